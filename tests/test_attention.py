@@ -1,0 +1,133 @@
+"""Fused SDPA forward + backward through F.scaled_dot_product_attention vs the float64 oracle
+(cases of the reference tests/test_fused_attention.py:29-169) and at BASELINE config 2."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from tests.helpers import ATTN_REL, rel_err, rnd_unit
+
+pytestmark = pytest.mark.gpu
+DTYPES = [torch.float32, torch.bfloat16, torch.float16]
+OVR = "aten::_scaled_dot_product_fused_attention_overrideable"
+SHAPES = [(1, 1, 32, 32, 64), (1, 2, 40, 50, 64), (2, 3, 33, 33, 40), (1, 4, 100, 77, 64), (1, 2, 64, 64, 128),
+          (1, 2, 17, 5, 20), (1, 2, 130, 130, 96), (1, 2, 35, 37, 30), (1, 1, 48, 48, 36)]
+
+
+@pytest.fixture(autouse=True)
+def tv():
+    import torch_vulkan_b200 as tv
+
+    tv.set_fused_attention("on")
+    tv.reset_counts()
+    yield tv
+    tv.set_fused_attention("auto")
+
+
+def run_dev(q, k, v, g):
+    qv, kv, vv = [t.cuda().requires_grad_(True) for t in (q, k, v)]
+    o = F.scaled_dot_product_attention(qv, kv, vv)
+    o.backward(g.cuda())
+    return o.detach().cpu(), qv.grad.cpu(), kv.grad.cpu(), vv.grad.cpu()
+
+
+def check_all(q, k, v, g, dtype, got):
+    o64, _ = oracle.sdpa_fwd(q, k, v)
+    dq64, dk64, dv64 = oracle.sdpa_bwd(q, k, v, g)
+    for name, x, ref in zip(("out", "dq", "dk", "dv"), got, (o64, dq64, dk64, dv64)):
+        assert x.dtype == dtype and x.shape == ref.shape, name
+        e = rel_err(x, ref)
+        assert e < ATTN_REL[dtype], f"{name}: rel err {e}"
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape", SHAPES)
+def test_fused_matches_oracle(tv, shape, dtype):
+    B, H, Sq, Sk, D = shape
+    q, k, v = rnd_unit((B, H, Sq, D), dtype, 1), rnd_unit((B, H, Sk, D), dtype, 2), rnd_unit((B, H, Sk, D), dtype, 3)
+    g = rnd_unit((B, H, Sq, D), dtype, 4)
+    check_all(q, k, v, g, dtype, run_dev(q, k, v, g))
+    kc = tv.kernel_counts()
+    assert kc.get(OVR, 0) >= 1 and kc.get(OVR + "_backward", 0) >= 1, kc
+    assert not any("softmax" in n or "bmm" in n for n in kc), kc
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_strided_bshd_inputs(tv, dtype):
+    B, H, S, D = 2, 4, 70, 64
+    qb, kb, vb, gb = (rnd_unit((B, S, H, D), dtype, 5 + i) for i in range(4))
+    q, k, v, g = (t.transpose(1, 2) for t in (qb, kb, vb, gb))
+    qv, kv, vv = (t.cuda().transpose(1, 2).detach().requires_grad_(True) for t in (qb, kb, vb))
+    o = F.scaled_dot_product_attention(qv, kv, vv)
+    o.backward(gb.cuda().transpose(1, 2))
+    check_all(q, k, v, g, dtype, (o.detach().cpu(), qv.grad.cpu(), kv.grad.cpu(), vv.grad.cpu()))
+    assert o.transpose(1, 2).is_contiguous()
+
+
+def test_large_logits_stay_fp32(tv):
+    B, H, S, D = 1, 2, 256, 64
+    q = rnd_unit((B, H, S, D), torch.bfloat16, 11, 6.0)
+    k = rnd_unit((B, H, S, D), torch.bfloat16, 12, 6.0)
+    v = rnd_unit((B, H, S, D), torch.bfloat16, 13)
+    got = F.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    assert rel_err(got, oracle.sdpa_fwd(q, k, v)[0]) < 6e-3
+
+
+def test_unsupported_cases_leave_the_fused_kernel(tv):
+    B, H, S = 1, 2, 24
+    q, k, v = (rnd_unit((B, H, S, 160), torch.float32, 21 + i) for i in range(3))
+    got = F.scaled_dot_product_attention(q.cuda(), k.cuda(), v.cuda()).cpu()
+    assert rel_err(got, oracle.sdpa_fwd(q, k, v)[0]) < 3e-5
+    mask = torch.zeros(S, S)
+    mask[:, S // 2:] = float("-inf")
+    q2, k2, v2 = (t[..., :64].contiguous() for t in (q, k, v))
+    ref2 = F.scaled_dot_product_attention(q2, k2, v2, attn_mask=mask)
+    got2 = F.scaled_dot_product_attention(q2.cuda(), k2.cuda(), v2.cuda(), attn_mask=mask.cuda()).cpu()
+    assert rel_err(got2, ref2) < 3e-5
+    assert tv.kernel_counts().get(OVR, 0) == 0
+
+
+def test_auto_policy(tv):
+    tv.set_fused_attention("auto")
+    q = rnd_unit((1, 2, 64, 64), torch.float32, 41)
+    F.scaled_dot_product_attention(q.cuda(), q.cuda(), q.cuda())
+    assert tv.kernel_counts().get(OVR, 0) == 0  # small fp32: not fused under auto
+    qb = q.to(torch.bfloat16).cuda()
+    F.scaled_dot_product_attention(qb, qb, qb)
+    assert tv.kernel_counts().get(OVR, 0) == 1
+    tv.set_fused_attention("off")
+    tv.reset_counts()
+    F.scaled_dot_product_attention(qb, qb, qb)
+    assert tv.kernel_counts().get(OVR, 0) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_unaligned_views(tv, dtype):
+    B, H, S, D = 1, 2, 45, 64
+    n = B * H * S * D
+    flats = [rnd_unit((n + 3,), dtype, 10 + i) for i in range(3)]
+    gflat = rnd_unit((n + 3,), dtype, 20)
+    views = [f[3:].reshape(B, H, S, D) for f in flats]
+    gv = gflat[3:].reshape(B, H, S, D)
+    q, k, v = (f.cuda()[3:].view(B, H, S, D).detach().requires_grad_(True) for f in flats)
+    o = F.scaled_dot_product_attention(q, k, v)
+    o.backward(gv.cuda())
+    check_all(*views, gv, dtype, (o.detach().cpu(), q.grad.cpu(), k.grad.cpu(), v.grad.cpu()))
+
+
+def test_config2_attention_and_tc_vs_simt(tv):
+    """B1 H16 S1024 D128 bf16, q/k/v/dO ~N(0,1), scale 1/sqrt(128)."""
+    g = torch.Generator().manual_seed(0)
+    q, k, v, do = (torch.randn(1, 16, 1024, 128, generator=g).to(torch.bfloat16) for _ in range(4))
+    got = run_dev(q, k, v, do)
+    check_all(q, k, v, do, torch.bfloat16, got)
+    tv.set_tc_attention_enabled(False)
+    try:
+        simt = run_dev(q, k, v, do)
+    finally:
+        tv.set_tc_attention_enabled(True)
+    for a, b in zip(got, simt):
+        assert rel_err(a, b) < 2e-2

@@ -1,0 +1,290 @@
+"""torch_vulkan_b200 — B200-native hot path of torch-vulkan, as a drop-in for CUDA tensors.
+
+Importing this package loads two native libraries built for sm_100a (see ``_build.py``):
+
+* ``libb2rt.so`` — the C ABI (``include/b2rt.h``): slab allocator, stream/launch layer, stats, and
+  every kernel (tcgen05 GEMM and int8-dequant GEMM, fused attention, softmax/LayerNorm row kernels,
+  optimizer ternaries);
+* ``_b2ops.so`` — the ATen shim that registers ``mm/bmm/addmm/baddbmm``, the SDPA
+  ``_fused_attention_overrideable`` pair, ``_softmax``/``_safe_softmax``/``_softmax_backward_data``,
+  ``native_layer_norm[_backward]`` and ``addcmul(_)/addcdiv(_)/lerp(_).Scalar`` for the CUDA key.
+
+The public functions mirror the reference package ``torch_vulkan/__init__.py`` (memory API 58-111,
+stats 155-213, ``dequant_int8`` 193-205, ``set_fused_attention`` 84-87, ``set_coop_enabled`` 253-266)
+with CUDA devices in place of the "vk" device. There is no CPU fallback: if the native libraries are
+missing the import fails.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libb2rt.so")
+_OPS_PATH = os.path.join(_HERE, "_b2ops.so")
+
+
+def _load():
+    missing = [p for p in (_LIB_PATH, _OPS_PATH) if not os.path.exists(p)]
+    if missing:
+        raise ImportError(
+            "torch_vulkan_b200: native libraries not built (missing: %s); run "
+            "`python -c 'import __graft_entry__ as g; g.build()'` or `python torch_vulkan_b200/_build.py`"
+            % ", ".join(os.path.basename(m) for m in missing)
+        )
+    lib = ctypes.CDLL(_LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+    torch.ops.load_library(_OPS_PATH)
+    return lib
+
+
+_lib = _load()
+_u64 = ctypes.c_uint64
+_lib.b2rt_live_bytes.restype = _u64
+_lib.b2rt_peak_live_bytes.restype = _u64
+_lib.b2rt_reserved_bytes.restype = _u64
+_lib.b2rt_max_alloc.restype = _u64
+_lib.b2rt_stat.restype = _u64
+_lib.b2rt_stat.argtypes = [ctypes.c_uint32]
+_lib.b2rt_set_memory_limit.argtypes = [_u64]
+_lib.b2rt_alloc.restype = _u64
+_lib.b2rt_alloc.argtypes = [_u64]
+_lib.b2rt_free.argtypes = [_u64]
+_lib.b2rt_empty_cache.restype = ctypes.c_size_t
+_lib.b2rt_live_blocks.restype = ctypes.c_size_t
+_lib.b2rt_slab_count.restype = ctypes.c_size_t
+_lib.b2rt_op_counts.restype = ctypes.c_size_t
+_lib.b2rt_profile_dump.restype = ctypes.c_size_t
+_lib.b2rt_last_error.restype = ctypes.c_size_t
+_lib.b2rt_device_name.restype = ctypes.c_size_t
+
+_STAT_NAMES = ["launches", "launch_ns", "upload_bytes", "download_bytes", "allocs", "frees", "sync_ns",
+               "cross_stream_waits"]
+
+
+def _text(fn) -> str:
+    n = fn(None, 0)
+    buf = ctypes.create_string_buffer(n + 1)
+    fn(buf, n + 1)
+    return buf.value.decode()
+
+
+def last_error() -> str:
+    return _text(_lib.b2rt_last_error)
+
+
+# ---- enable / disable the operator overrides ---------------------------------------------------
+
+def enable(on: bool = True) -> None:
+    """Register (or remove) the hot-path kernels for CUDA tensors. Removing restores PyTorch's own CUDA
+    kernels, which makes A/B comparisons possible in one process."""
+    torch.ops.b2.set_enabled(bool(on))
+
+
+def is_enabled() -> bool:
+    return bool(torch.ops.b2.is_enabled())
+
+
+# ---- device API (torch_vulkan/__init__.py:34-56) -----------------------------------------------
+
+def is_available() -> bool:
+    return torch.cuda.is_available()
+
+
+def device_count() -> int:
+    return torch.cuda.device_count()
+
+
+def current_device() -> int:
+    return torch.cuda.current_device()
+
+
+def synchronize(device=None) -> None:
+    torch.cuda.synchronize(device)
+
+
+def device_name() -> str:
+    return _text(_lib.b2rt_device_name)
+
+
+# ---- memory API (torch_vulkan/__init__.py:58-111) ----------------------------------------------
+# These report the slab allocator of libb2rt (used by b2rt_alloc and, after use_slab_allocator(),
+# by every CUDA tensor).
+
+def live_bytes() -> int:
+    return int(_lib.b2rt_live_bytes())
+
+
+def memory_info() -> dict:
+    out = (_u64 * 3)()
+    rc = _lib.b2rt_memory_info(out)
+    if rc != 0:
+        raise RuntimeError("memory_info: " + last_error())
+    return {"budget": int(out[0]), "usage": int(out[1]), "heap": int(out[2])}
+
+
+def peak_live_bytes() -> int:
+    return int(_lib.b2rt_peak_live_bytes())
+
+
+def reset_peak_live_bytes() -> None:
+    _lib.b2rt_reset_peak_live_bytes()
+
+
+def set_memory_limit(megabytes: int) -> None:
+    """Cap the slab allocator's reserved bytes (MiB, 0 = none) to emulate a smaller GPU."""
+    _lib.b2rt_set_memory_limit(int(megabytes) << 20)
+
+
+def empty_cache() -> None:
+    _lib.b2rt_empty_cache()
+
+
+def reserved_bytes() -> int:
+    return int(_lib.b2rt_reserved_bytes())
+
+
+def live_blocks() -> int:
+    return int(_lib.b2rt_live_blocks())
+
+
+def slab_count() -> int:
+    return int(_lib.b2rt_slab_count())
+
+
+_slab_installed = False
+
+
+def use_slab_allocator() -> None:
+    """Route every CUDA tensor allocation through the slab allocator (b2_malloc / b2_free), the
+    counterpart of the reference's c10::Allocator over vkrt (csrc/shim.cpp:154-171). Must run before
+    the first CUDA allocation of the process."""
+    global _slab_installed
+    if _slab_installed:
+        return
+    alloc = torch.cuda.memory.CUDAPluggableAllocator(_LIB_PATH, "b2_malloc", "b2_free")
+    torch.cuda.memory.change_current_allocator(alloc)
+    _slab_installed = True
+
+
+# ---- stats (torch_vulkan/__init__.py:155-213) --------------------------------------------------
+
+def stats() -> dict:
+    return {name: int(_lib.b2rt_stat(i)) for i, name in enumerate(_STAT_NAMES)}
+
+
+def _counts() -> dict:
+    out = {}
+    for line in _text(_lib.b2rt_op_counts).splitlines():
+        if line:
+            k, v = line.rsplit("\t", 1)
+            out[k] = int(v)
+    return out
+
+
+def kernel_counts() -> dict:
+    """Operator name -> number of calls served by this library's kernels."""
+    return {k: v for k, v in _counts().items() if not k.startswith("fallback:")}
+
+
+def fallback_counts() -> dict:
+    """Operator name -> number of calls that took PyTorch's stock CUDA path (uncovered dtypes)."""
+    return {k[len("fallback:"):]: v for k, v in _counts().items() if k.startswith("fallback:")}
+
+
+def reset_fallback_counts() -> None:
+    _lib.b2rt_reset_op_counts()
+
+
+reset_counts = reset_fallback_counts
+
+
+def validation_errors() -> int:
+    """Device-side error word (bounded waits that expired); 0 when every kernel completed normally.
+    The counterpart of the reference's Vulkan validation-error counter."""
+    return int(_lib.b2rt_device_error(0))
+
+
+def profile_enable(on: bool = True) -> None:
+    _lib.b2rt_profile_enable(1 if on else 0)
+
+
+def profile() -> str:
+    """'name\\tms\\tcount' lines of per-kernel GPU time (after profile_enable or B2RT_PROFILE=1)."""
+    return _text(_lib.b2rt_profile_dump)
+
+
+# ---- kernel switches (torch_vulkan/__init__.py:84-87, 253-266) -----------------------------------
+
+def set_fused_attention(mode: str) -> None:
+    """Fused attention policy: "auto" (default), "on" or "off" (env B2_FUSED_ATTN=0/1)."""
+    torch.ops.b2.set_fused_attention({"off": 0, "on": 1, "auto": 2}[mode])
+
+
+_force = 0
+
+
+def set_coop_enabled(on: bool) -> None:
+    """True (default): bf16/f16 GEMMs use the tcgen05 tensor-core kernel; False: the strided SIMT
+    kernel (the reference's coop/tiled switch, used to A/B kernels)."""
+    global _force
+    _force = (_force & ~1) | (0 if on else 1)
+    torch.ops.b2.set_force_simt(_force)
+
+
+def set_tc_attention_enabled(on: bool) -> None:
+    """True (default): eligible attention uses the tcgen05 kernels; False: the SIMT kernels."""
+    global _force
+    _force = (_force & ~2) | (0 if on else 2)
+    torch.ops.b2.set_force_simt(_force)
+
+
+def coop_caps() -> int:
+    """bit0 = f16, bit1 = bf16 tensor-core GEMM available (sm_100a device present)."""
+    return 3 if torch.cuda.is_available() and torch.cuda.get_device_capability() == (10, 0) else 0
+
+
+def gemm_path(a: torch.Tensor, b: torch.Tensor) -> str:
+    return "tcgen05" if int(torch.ops.b2.gemm_path(a, b)) == 1 else "simt"
+
+
+# ---- int8 weight-only quantisation ---------------------------------------------------------------
+
+def dequant_int8(q: torch.Tensor, scale: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """out[r, c] = float(q[r, c]) * float(scale) rounded to out_dtype (round-to-nearest-even).
+
+    scale is bf16 [rows, ceil(cols/64)] (one scale per 64-column block, the reference layout of
+    torch_vulkan/__init__.py:193-205) or fp32 [rows] (per output row). CUDA tensors only."""
+    if not q.is_cuda:
+        raise RuntimeError("dequant_int8: q must be a CUDA tensor (this package has no CPU path)")
+    return torch.ops.b2.dequant_int8(q, scale, out_dtype)
+
+
+class _Int8Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, q, scale, bias):
+        ctx.save_for_backward(q, scale)
+        ctx.has_bias = bias is not None
+        return torch.ops.b2.int8_linear_fwd(x, q, scale, bias)
+
+    @staticmethod
+    def backward(ctx, gy):
+        q, scale = ctx.saved_tensors
+        gx = torch.ops.b2.int8_linear_dx(gy.contiguous(), q, scale) if ctx.needs_input_grad[0] else None
+        gb = gy.reshape(-1, gy.shape[-1]).sum(0) if (ctx.has_bias and ctx.needs_input_grad[3]) else None
+        return gx, None, None, gb
+
+
+def int8_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor | None = None):
+    """y = x @ (q * scale)^T + bias with the dequantisation fused into the tcgen05 GEMM mainloop.
+    Differentiable in x (and bias); q/scale are frozen. x bf16 [..., K], q int8 [N, K]."""
+    return _Int8Linear.apply(x, q, scale, bias)
+
+
+if os.environ.get("B2_DISABLE", "0") in ("", "0"):
+    enable(True)
+
+if os.environ.get("B2_MEM_LIMIT_MB"):
+    set_memory_limit(int(os.environ["B2_MEM_LIMIT_MB"]))

@@ -1,0 +1,567 @@
+// Tensor-core GEMM for sm_100a: tcgen05.mma with TMEM accumulators, operands staged by TMA.
+//
+// Serves b2_gemm for bf16/f16 (the reference's cooperative-matrix kernel
+// vkrt/shaders/mm_coop.comp.in:96-209, 64x64x32 tiles, no double buffering) and b2_int8_gemm,
+// the int8-weight linear with the dequantisation fused into the mainloop (new: the reference
+// dequantises in a separate pass, vkrt/shaders/dq8.comp.in, then runs the GEMM).
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A and B tiles (128B-swizzled, K- or MN-major) into an S-stage ring
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma 128xBNx16 into a double-buffered
+//               fp32 accumulator (2*BN TMEM columns) and commits stages / accumulators to mbarriers
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, alpha/beta/bias, round, store to HBM,
+//               overlapped with the next tile's mainloop through the second accumulator
+//   warps 6..9  (int8 only) dequant: int8 tile (TMA, unswizzled) * scale -> bf16 (RNE) written
+//               straight into the swizzled UMMA layout of the B stage, bit-identical to
+//               b2_dequant_int8; the bf16 weight never reaches HBM
+// Every mbarrier wait is bounded (tc::kWaitLimitNs); on expiry the kernel records an error code,
+// drains its own TMA copies (bounded) and frees TMEM before returning.
+#include <cuda.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "tc_ptx.cuh"
+
+namespace b2 {
+
+// ---- driver entry point for tensor-map encoding (no -lcuda needed) ------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+    (void)cudaGetLastError();
+  });
+  return fn;
+}
+
+// Encodes a 2-D or 3-D tiled tensor map. dims/strides: innermost first; strides in bytes for dims
+// 1.. (dim 0 is contiguous). Returns false if the driver rejects it.
+bool make_tmap(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return false;
+  cuuint64_t gd[3], gs[2];
+  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  CUresult r = f(m, dt, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+
+struct TcParams {
+  int64_t M, N, K, batch;
+  int m_tiles, n_tiles, k_blocks;
+  int a_mn, b_mn;  // operand is MN-major (else K-major)
+  int a3d, b3d;    // tensor map has a batch dimension
+  void* c;
+  int64_t c_sb, c_sm, c_sn;
+  const void* bias;
+  int64_t bias_sb, bias_sm, bias_sn;
+  int has_bias;
+  float alpha, beta;
+  int* err;
+  // int8 dequant of B
+  const void* scale;
+  int scale_layout;
+  int64_t scale_nb;   // columns of the block-64 scale matrix
+  int64_t deq_rows;   // rows of q (output features N of the linear)
+};
+
+template <int BN, int DEQ>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int R_BYTES = DEQ ? BN * BK : 0;  // raw int8 tile
+  static constexpr int STAGE = A_BYTES + B_BYTES + R_BYTES;
+  static constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  static constexpr int THREADS = DEQ ? 320 : 192;
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+__device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int BN, bool BF16, int DEQ>
+__global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  using C = Cfg<BN, DEQ>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::STAGE);
+  uint64_t* full = bars;            // [S]  TMA landed
+  uint64_t* empty = bars + S;       // [S]  MMA done reading the stage
+  uint64_t* tfull = bars + 2 * S;   // [2]  accumulator ready
+  uint64_t* tempty = bars + 2 * S + 2;  // [2] accumulator drained
+  uint64_t* bready = bars + 2 * S + 4;  // [S] (int8) B stage dequantised
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_tiles = p.m_tiles * p.n_tiles * (int)p.batch;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], 1);
+      tc::mbar_init(&bready[i], 128);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&tfull[i], 1);
+      tc::mbar_init(&tempty[i], 128);
+    }
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  auto tile_coords = [&](int t, int& m0, int& n0, int& b) {
+    int per_b = p.m_tiles * p.n_tiles;
+    b = t / per_b;
+    int r = t - b * per_b;
+    int mt = r % p.m_tiles, nt = r / p.m_tiles;
+    m0 = mt * BM;
+    n0 = nt * BN;
+  };
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------------------
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&tmA);
+      tc::tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int m0, n0, b;
+        tile_coords(t, m0, n0, b);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, p.err) || *abort_flag) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE;
+          uint8_t* sb = sa + C::A_BYTES;
+          uint8_t* sr = sb + C::B_BYTES;
+          const uint32_t bytes = C::A_BYTES + (DEQ ? C::R_BYTES : C::B_BYTES);
+          tc::mbar_arrive_expect_tx(&full[stage], bytes);
+          const int k0 = kb * BK;
+          if (!p.a_mn) {
+            if (p.a3d) tc::tma_load_3d(sa, &tmA, &full[stage], k0, m0, b);
+            else tc::tma_load_2d(sa, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) {
+              if (p.a3d) tc::tma_load_3d(sa + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0, b);
+              else tc::tma_load_2d(sa + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
+            }
+          }
+          if (DEQ) {
+            // raw int8 W tile: forward box {64 (k), BN (n)}; transposed box {BN (k_feat), 64 (n_feat)}
+            if (!p.b_mn) tc::tma_load_2d(sr, &tmB, &full[stage], k0, n0);
+            else tc::tma_load_2d(sr, &tmB, &full[stage], n0, k0);
+          } else if (!p.b_mn) {
+            if (p.b3d) tc::tma_load_3d(sb, &tmB, &full[stage], k0, n0, b);
+            else tc::tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              if (p.b3d) tc::tma_load_3d(sb + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0, b);
+              else tc::tma_load_2d(sb + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+            }
+          }
+          issued[stage] += 1;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: every issued load completes on its stage's full barrier. Stage s saw issued[s]
+        // arms, so its phase count is issued[s]; wait (bounded) for the last one.
+        for (int s = 0; s < S; ++s)
+          if (issued[s] > 0) tc::mbar_wait(&full[s], (uint32_t)((issued[s] - 1) & 1), nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer ---------------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t IDESC_BASE = tc::idesc_f16(BM, BN, BF16, false, false);
+      const uint32_t idesc = IDESC_BASE | ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        if (!tc::mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!tc::mbar_wait(&full[stage], phase, p.err) || (DEQ && !tc::mbar_wait(&bready[stage], phase, p.err))) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          uint8_t* sa = smem + stage * C::STAGE;
+          uint8_t* sb = sa + C::A_BYTES;
+          const uint32_t a_addr = tc::smem_u32(sa), b_addr = tc::smem_u32(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: +32 B per 16-element K step inside the 128 B swizzle row.
+            // MN-major: +16 rows of 128 B per step; LBO = distance between 64-element MN chunks.
+            uint64_t ad = p.a_mn ? tc::sdesc_sw128(a_addr + k * 2048, 8192, 1024) : tc::sdesc_sw128(a_addr + k * 32, 16, 1024);
+            uint64_t bd = p.b_mn ? tc::sdesc_sw128(b_addr + k * 2048, 8192, 1024) : tc::sdesc_sw128(b_addr + k * 32, 16, 1024);
+            tc::mma_f16_ss(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc::mma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc::mma_commit(&tfull[acc]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp < 6) {
+    // ------------------------------- epilogue -----------------------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      if (!tc::mbar_wait(&tfull[acc], (it >> 1) & 1, p.err) || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      tc::tc_fence_after();
+      int m0, n0, b;
+      tile_coords(t, m0, n0, b);
+      const int64_t row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      OutT* crow = (OutT*)p.c + b * p.c_sb + row * p.c_sm;
+      const OutT* brow = (const OutT*)p.bias + b * p.bias_sb + row * p.bias_sm;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t r[32];
+        __syncwarp();
+        tc::tmem_ld32(tbase + (uint32_t)(acc * BN + ch * 32) + ((uint32_t)(q * 32) << 16), r);
+        tc::tmem_wait_ld();
+        const int64_t col0 = n0 + ch * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+        if (p.has_bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) v[j] += p.beta * to_f32(brow[(col0 + j) * p.bias_sn]);
+        }
+        const bool vec = (p.c_sn == 1) && (col0 + 32 <= p.N) && ((reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0);
+        if (vec) {
+          uint4* dst = reinterpret_cast<uint4*>(crow + col0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_uint4(pack_out(v[8 * j], v[8 * j + 1], BF16), pack_out(v[8 * j + 2], v[8 * j + 3], BF16),
+                                pack_out(v[8 * j + 4], v[8 * j + 5], BF16), pack_out(v[8 * j + 6], v[8 * j + 7], BF16));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) crow[(col0 + j) * p.c_sn] = from_f32<OutT>(v[j]);
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&tempty[acc]);
+    }
+  } else if (DEQ) {
+    // ------------------------------- int8 dequant -------------------------------------------
+    const int dt = threadIdx.x - 6 * 32;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      int m0, n0, b;
+      tile_coords(t, m0, n0, b);
+      bool ok = true;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!tc::mbar_wait(&full[stage], phase, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        uint8_t* sb = smem + stage * C::STAGE + C::A_BYTES;
+        const uint8_t* sr = sb + C::B_BYTES;
+        if (!p.b_mn) {
+          // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
+          // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
+          for (int i = dt; i < BN * 4; i += 128) {
+            const int n = i >> 2, j = i & 3;  // 16 int8 = k 16j..16j+15
+            const int64_t gn = (int64_t)n0 + n;
+            float s = 0.f;
+            if (gn < p.deq_rows)
+              s = p.scale_layout == 0
+                      ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
+                      : reinterpret_cast<const float*>(p.scale)[gn];
+            int4 raw = *reinterpret_cast<const int4*>(sr + n * 64 + j * 16);
+            const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+            uint32_t w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              w[e] = (uint32_t)f32_to_bf16_bits((float)qb[2 * e] * s) |
+                     ((uint32_t)f32_to_bf16_bits((float)qb[2 * e + 1] * s) << 16);
+            uint8_t* rowp = sb + n * 128;
+            const int c0 = 2 * j, c1 = 2 * j + 1;
+            *reinterpret_cast<uint4*>(rowp + ((c0 ^ (n & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(rowp + ((c1 ^ (n & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+        } else {
+          // backward: raw [64 rows i (n_feat)][BN bytes (k_feat = n_gemm)]; B stage MN-major SW128:
+          // chunk j = n_gemm/64 at j*8192, row i at i*128, 16 B granule g at ((g ^ (i & 7)) * 16).
+          for (int e = dt; e < 64 * (BN / 16); e += 128) {
+            const int i = e / (BN / 16), qd = e % (BN / 16);
+            const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
+            const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
+            float s = 0.f;
+            if (nf < p.deq_rows)
+              s = p.scale_layout == 0
+                      ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
+                      : reinterpret_cast<const float*>(p.scale)[nf];
+            int4 raw = *reinterpret_cast<const int4*>(sr + i * BN + qd * 16);
+            const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+            uint32_t w[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x)
+              w[x] = (uint32_t)f32_to_bf16_bits((float)qb[2 * x] * s) |
+                     ((uint32_t)f32_to_bf16_bits((float)qb[2 * x + 1] * s) << 16);
+            const int chunk = (qd * 16) >> 6, g0 = ((qd * 16) & 63) >> 3;
+            uint8_t* rowp = sb + chunk * 8192 + i * 128;
+            *reinterpret_cast<uint4*>(rowp + ((g0 ^ (i & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<uint4*>(rowp + (((g0 + 1) ^ (i & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+        }
+        tc::fence_async_shared();
+        tc::mbar_arrive(&bready[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------------------
+
+bool tma_ok_stride(int64_t s_elems, int esz) { return ((s_elems * esz) % 16) == 0; }
+
+template <int BN, bool BF16, int DEQ>
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t st, const char* name) {
+  using C = Cfg<BN, DEQ>;
+  static bool attr_set = false;  // set once per process (single device per process)
+  if (!attr_set) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<BN, BF16, DEQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::SMEM),
+                            "cudaFuncSetAttribute(gemm_tc)"))
+      return rc;
+    attr_set = true;
+  }
+  int tiles = p.m_tiles * p.n_tiles * (int)p.batch;
+  int grid = std::min(tiles, device_info().sm_count);
+  LaunchScope ls(name, st);
+  gemm_tc_kernel<BN, BF16, DEQ><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
+  return after_launch(name);
+}
+
+// Wave-quantisation aware choice between 128- and 256-wide tiles.
+int pick_bn(int64_t M, int64_t N, int64_t batch) {
+  const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
+  auto score = [&](int bn, double tile_eff) {
+    int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn) * batch;
+    int64_t waves = (tiles + sms - 1) / sms;
+    double useful = (double)M * N * batch;
+    double work = (double)waves * sms * BM * bn;
+    return useful / work * tile_eff;
+  };
+  return score(256, 1.0) >= score(128, 0.92) ? 256 : 128;
+}
+
+}  // namespace
+
+bool gemm_tc_eligible(const b2_gemm_args* a) {
+  if (a->dtype != B2_BF16 && a->dtype != B2_F16) return false;
+  if (!device_info().tcgen05 || !encode_fn()) return false;
+  if (a->K <= 0 || a->M <= 0 || a->N <= 0) return false;
+  const int e = 2;
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (!al(a->a) || !al(a->b)) return false;
+  // A: K-major (a_sk == 1) or M-major (a_sm == 1); the other stride must be a 16-byte multiple
+  bool a_k = a->a_sk == 1 && (a->M == 1 || tma_ok_stride(a->a_sm, e));
+  bool a_m = !a_k && a->a_sm == 1 && (a->K == 1 || tma_ok_stride(a->a_sk, e));
+  bool b_k = a->b_sk == 1 && (a->N == 1 || tma_ok_stride(a->b_sn, e));
+  bool b_n = !b_k && a->b_sn == 1 && (a->K == 1 || tma_ok_stride(a->b_sk, e));
+  if (!(a_k || a_m) || !(b_k || b_n)) return false;
+  if (a->batch > 1) {
+    if (a->a_sb != 0 && !tma_ok_stride(a->a_sb, e)) return false;
+    if (a->b_sb != 0 && !tma_ok_stride(a->b_sb, e)) return false;
+  }
+  // TMA dims/strides must fit the encoder's 32-bit box coordinates
+  if (a->M >= (1ll << 31) || a->N >= (1ll << 31) || a->K >= (1ll << 31)) return false;
+  return true;
+}
+
+int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
+  const bool bf16 = a->dtype == B2_BF16;
+  const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int BN = pick_bn(a->M, a->N, a->batch);
+  TcParams p{};
+  p.M = a->M, p.N = a->N, p.K = a->K, p.batch = a->batch;
+  p.m_tiles = (int)((a->M + BM - 1) / BM);
+  p.n_tiles = (int)((a->N + BN - 1) / BN);
+  p.k_blocks = (int)((a->K + BK - 1) / BK);
+  p.a_mn = !(a->a_sk == 1 && (a->M == 1 || tma_ok_stride(a->a_sm, 2)));
+  p.b_mn = !(a->b_sk == 1 && (a->N == 1 || tma_ok_stride(a->b_sn, 2)));
+  p.a3d = a->batch > 1 && a->a_sb != 0;
+  p.b3d = a->batch > 1 && a->b_sb != 0;
+  p.c = a->c, p.c_sb = a->c_sb, p.c_sm = a->c_sm, p.c_sn = a->c_sn;
+  p.bias = a->bias, p.has_bias = a->has_bias && a->bias != nullptr;
+  p.bias_sb = a->bias_sb, p.bias_sm = a->bias_sm, p.bias_sn = a->bias_sn;
+  p.alpha = a->alpha, p.beta = a->beta;
+  p.err = device_error_ptr();
+
+  CUtensorMap ta, tb;
+  {
+    uint64_t dims[3], strides[2];
+    uint32_t box[3];
+    int rank = p.a3d ? 3 : 2;
+    if (!p.a_mn) {
+      dims[0] = a->K, dims[1] = a->M, strides[0] = (uint64_t)(a->M == 1 ? a->K : a->a_sm) * 2;
+      box[0] = 64, box[1] = BM;
+    } else {
+      dims[0] = a->M, dims[1] = a->K, strides[0] = (uint64_t)(a->K == 1 ? a->M : a->a_sk) * 2;
+      box[0] = 64, box[1] = 64;
+    }
+    if (strides[0] == 0 || strides[0] % 16) strides[0] = ((dims[0] * 2 + 15) / 16) * 16;
+    dims[2] = a->batch, strides[1] = (uint64_t)a->a_sb * 2, box[2] = 1;
+    if (!make_tmap(&ta, dt, rank, a->a, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(B2_ERR_ARG, "gemm_tc: tensor map for A rejected");
+  }
+  {
+    uint64_t dims[3], strides[2];
+    uint32_t box[3];
+    int rank = p.b3d ? 3 : 2;
+    if (!p.b_mn) {
+      dims[0] = a->K, dims[1] = a->N, strides[0] = (uint64_t)(a->N == 1 ? a->K : a->b_sn) * 2;
+      box[0] = 64, box[1] = BN;
+    } else {
+      dims[0] = a->N, dims[1] = a->K, strides[0] = (uint64_t)(a->K == 1 ? a->N : a->b_sk) * 2;
+      box[0] = 64, box[1] = 64;
+    }
+    if (strides[0] == 0 || strides[0] % 16) strides[0] = ((dims[0] * 2 + 15) / 16) * 16;
+    dims[2] = a->batch, strides[1] = (uint64_t)a->b_sb * 2, box[2] = 1;
+    if (!make_tmap(&tb, dt, rank, a->b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(B2_ERR_ARG, "gemm_tc: tensor map for B rejected");
+  }
+  if (BN == 256)
+    return bf16 ? launch_kernel<256, true, 0>(ta, tb, p, st, "gemm_tc_bn256") : launch_kernel<256, false, 0>(ta, tb, p, st, "gemm_tc_bn256");
+  return bf16 ? launch_kernel<128, true, 0>(ta, tb, p, st, "gemm_tc_bn128") : launch_kernel<128, false, 0>(ta, tb, p, st, "gemm_tc_bn128");
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+// ---- fused int8-weight linear -------------------------------------------------------------------
+extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
+  if (!a) return fail(B2_ERR_ARG, "int8_gemm: null args");
+  if (int rc = ensure_init()) return rc;
+  if (a->M < 0 || a->N < 0 || a->K < 0) return fail(B2_ERR_ARG, "int8_gemm: negative size");
+  if (a->scale_layout != 0 && a->scale_layout != 1) return fail(B2_ERR_ARG, "int8_gemm: scale_layout must be 0 or 1");
+  const int64_t out_cols = a->transpose_w ? a->K : a->N;
+  const int64_t red = a->transpose_w ? a->N : a->K;  // reduction length
+  if (a->M == 0 || out_cols == 0) return 0;
+  if (!a->x || !a->q || !a->scale || !a->out) return fail(B2_ERR_ARG, "int8_gemm: null pointer");
+  if (!device_info().tcgen05 || !encode_fn()) return fail(B2_ERR_ARG, "int8_gemm: requires an sm_100a device");
+  if (red == 0) return fail(B2_ERR_ARG, "int8_gemm: empty reduction");
+  if (((uintptr_t)a->x & 15) || ((uintptr_t)a->q & 15) || a->x_ld % 8 || a->K % 16)
+    return fail(B2_ERR_ARG, "int8_gemm: x and q must be 16-byte aligned, x_ld a multiple of 8 and K of 16");
+  if (a->transpose_w && a->bias) return fail(B2_ERR_ARG, "int8_gemm: bias is only supported in the forward form");
+  cudaStream_t st = (cudaStream_t)stream;
+  constexpr int BN = 256;  // a wide W tile amortises the dequant over more of the M tile
+  TcParams p{};
+  p.M = a->M, p.N = out_cols, p.K = red, p.batch = 1;
+  p.m_tiles = (int)((a->M + BM - 1) / BM);
+  p.n_tiles = (int)((out_cols + BN - 1) / BN);
+  p.k_blocks = (int)((red + BK - 1) / BK);
+  p.a_mn = 0;
+  p.b_mn = a->transpose_w ? 1 : 0;
+  p.c = a->out, p.c_sm = a->out_ld, p.c_sn = 1, p.c_sb = 0;
+  p.bias = a->bias, p.has_bias = a->bias != nullptr, p.bias_sn = 1;
+  p.alpha = 1.f, p.beta = 1.f;
+  p.err = device_error_ptr();
+  p.scale = a->scale, p.scale_layout = a->scale_layout, p.scale_nb = (a->K + 63) / 64, p.deq_rows = a->N;
+  CUtensorMap ta, tb;
+  {
+    uint64_t dims[2] = {(uint64_t)red, (uint64_t)a->M}, strides[1] = {(uint64_t)a->x_ld * 2};
+    uint32_t box[2] = {64, BM};
+    if (!make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(B2_ERR_ARG, "int8_gemm: tensor map for x rejected");
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)a->K, (uint64_t)a->N}, strides[1] = {(uint64_t)a->K};
+    uint32_t box[2];
+    if (!a->transpose_w) box[0] = 64, box[1] = BN;
+    else box[0] = BN, box[1] = 64;
+    if (!make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return fail(B2_ERR_ARG, "int8_gemm: tensor map for q rejected");
+  }
+  return launch_kernel<BN, true, 1>(ta, tb, p, st, a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd");
+}
