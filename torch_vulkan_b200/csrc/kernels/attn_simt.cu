@@ -314,6 +314,15 @@ int check_args(const b2_attn_args* a, bool bwd) {
 
 }  // namespace
 
+// SIMT backward, also used by attn_tc.cu for cases its kernels do not take.
+int attn_simt_bwd_dispatch(const b2_attn_args* a, cudaStream_t st) {
+  switch (a->dtype) {
+    case B2_F32: return simt_bwd<float>(a, st);
+    case B2_BF16: return simt_bwd<__nv_bfloat16>(a, st);
+    default: return simt_bwd<__half>(a, st);
+  }
+}
+
 // Entry points shared with attn_tc.cu for its delta pre-pass.
 int attn_delta_launch(const b2_attn_args* a, cudaStream_t st) {
   switch (a->dtype) {

@@ -1,11 +1,778 @@
-// Tensor-core attention (tcgen05) — placeholder until the sm_100a kernels land: nothing is eligible,
-// so b2_attn_fwd/bwd route every case to the SIMT kernels.
+// Tensor-core fused attention for sm_100a (tcgen05 + TMEM + TMA), bf16/f16, head dim 64 or 128.
+//
+// Replaces the reference's cooperative-matrix kernels vkrt/shaders/attn_coop.comp.in (fwd 158-211,
+// dK/dV 213-259, dQ 261-301) and the delta pass attn.comp.in:210-240. Same equations
+// (FlashAttention-2): forward online softmax with lse = m + log(l); backward
+// P = exp(scale*S - lse), dS = P*(dP - delta), dV = P^T dO, dK = scale dS^T Q, dQ = scale dS K.
+// B200 design:
+//  forward  one CTA per (128-query tile, batch*head). warp 0 TMA (Q once, K/V ring), warp 1 issues
+//           S = Q K^T into a double-buffered TMEM tile and O += P V into a TMEM accumulator, warps
+//           2..5 (one thread per query row) run the online softmax from tcgen05.ld'ed S, write P
+//           (bf16, 128B-swizzled) to shared memory for the PV MMA, and rescale O in TMEM only when the
+//           running max grows by more than 2^8 (lazy rescaling); the epilogue normalises O from TMEM.
+//  backward delta = rowsum(O*dO) pre-pass; then one CTA per (128-key tile, batch*head) keeps K, V in
+//           shared memory and dK, dV in TMEM while it walks 64-query tiles: S^T = K Q^T and
+//           dP^T = V dO^T on the tensor cores, P^T / dS^T in registers (thread = key row), then
+//           dV += P^T dO, dK += dS^T Q and dQ^T = K^T dS^T (all tcgen05); dQ partials are added into an
+//           fp32 workspace with vector atomics and converted at the end.
+// Every mbarrier wait is bounded; on expiry the kernel records an error code and unwinds.
+#include <cuda.h>
+
+#include <type_traits>
+
 #include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace b2 {
-bool attn_tc_eligible(const b2_attn_args*) { return false; }
-int attn_tc_fwd(const b2_attn_args*, cudaStream_t) { return fail(B2_ERR_ARG, "attn_tc: not available"); }
-int attn_tc_bwd(const b2_attn_args*, cudaStream_t) { return fail(B2_ERR_ARG, "attn_tc: not available"); }
+
+bool make_tmap(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw);  // gemm_tc.cu
+int attn_delta_launch(const b2_attn_args* a, cudaStream_t st);                              // attn_simt.cu
+
+namespace {
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Writes 8 packed pairs (16 elements) of row `r` into a K-major 128B-swizzled tile whose rows hold
+// 64 elements: granules g0, g0+1 of chunk `chunk` (chunk stride `chunk_bytes`).
+__device__ __forceinline__ void st_sw128_pair(uint8_t* tile, int chunk, int chunk_bytes, int r, int g0,
+                                              const uint32_t* w) {
+  uint8_t* row = tile + chunk * chunk_bytes + r * 128;
+  *reinterpret_cast<uint4*>(row + (((g0) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(row + (((g0 + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+struct AttnTcParams {
+  int64_t B, H, Sq, Sk;
+  float scale_log2;  // scale * log2(e)
+  float scale;
+  void* o;
+  int64_t o_s[3];
+  float* lse;
+  int* err;
+  // backward
+  const float* delta;
+  float* dq_acc;  // fp32 [B*H, Sq, D]
+  void* dk;
+  void* dv;
+  int64_t dk_s[3], dv_s[3];
+};
+
+// ==================================================================================================
+// forward
+// ==================================================================================================
+template <int D>
+struct FwdCfg {
+  static constexpr int BQ = 128, BKV = 128;
+  static constexpr int DCH = D / 64;                 // 64-element chunks along D
+  static constexpr int Q_BYTES = BQ * D * 2;         // 32 KB (D=128)
+  static constexpr int K_BYTES = BKV * D * 2;
+  static constexpr int V_BYTES = BKV * D * 2;
+  static constexpr int P_BYTES = BQ * BKV * 2;       // 32 KB
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;      // 2 stages
+  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;  // 2 stages
+  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;  // 2 buffers
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int THREADS = 192;
+  static constexpr uint32_t TMEM_COLS = 512;          // S0 [0,128) S1 [128,256) O [256, 256+D)
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
+  using C = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bar + 0;
+  uint64_t* k_full = bar + 1;   // [2]
+  uint64_t* k_empty = bar + 3;  // [2]
+  uint64_t* v_full = bar + 5;   // [2]
+  uint64_t* v_empty = bar + 7;  // [2]
+  uint64_t* s_full = bar + 9;   // [2]
+  uint64_t* p_full = bar + 11;  // [2]
+  uint64_t* o_upd = bar + 13;   // PV done (one phase per KV block)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 15);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * C::BQ;
+  const int bh = blockIdx.y;
+  const int b = bh / (int)p.H, h = bh % (int)p.H;
+  const int nblk = (int)((p.Sk + C::BKV - 1) / C::BKV);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&k_full[i], 1);
+      tc::mbar_init(&k_empty[i], 1);
+      tc::mbar_init(&v_full[i], 1);
+      tc::mbar_init(&v_empty[i], 1);
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&p_full[i], 128);
+    }
+    tc::mbar_init(o_upd, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t t_o = tbase + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer: Q once, then K_j / V_j into 2-stage rings ----------------
+      bool ok = true;
+      tc::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int c = 0; c < C::DCH; ++c) tc::tma_load_4d(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, q_full, c * 64, q0, h, b);
+      int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        if (!tc::mbar_wait(&k_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
+        tc::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
+        for (int c = 0; c < C::DCH; ++c)
+          tc::tma_load_4d(smem + C::OFF_K + s * C::K_BYTES + c * (C::BKV * 128), &tmK, &k_full[s], c * 64, j * C::BKV, h, b);
+        issued_k[s]++;
+        if (!tc::mbar_wait(&v_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
+        tc::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
+        for (int c = 0; c < C::DCH; ++c)
+          tc::tma_load_4d(smem + C::OFF_V + s * C::V_BYTES + c * (C::BKV * 128), &tmV, &v_full[s], c * 64, j * C::BKV, h, b);
+        issued_v[s]++;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        tc::mbar_wait(q_full, 0, nullptr);
+        for (int s = 0; s < 2; ++s) {
+          if (issued_k[s]) tc::mbar_wait(&k_full[s], (uint32_t)((issued_k[s] - 1) & 1), nullptr);
+          if (issued_v[s]) tc::mbar_wait(&v_full[s], (uint32_t)((issued_v[s] - 1) & 1), nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t IDESC_S = tc::idesc_f16(128, C::BKV, BF16, false, false);  // Q K^T: both K-major
+      constexpr uint32_t IDESC_O = tc::idesc_f16(128, D, BF16, false, true);        // P V: V is MN-major
+      const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q);
+      bool ok = tc::mbar_wait(q_full, 0, p.err);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&k_full[s], (uint32_t)((j >> 1) & 1), p.err)) return false;
+        tc::tc_fence_after();
+        const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K + s * C::K_BYTES);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * (128 * 128) + (k & 3) * 32;
+          tc::mma_f16_ss(tbase + s * 128, tc::sdesc_sw128(q_addr + off, 16, 1024),
+                         tc::sdesc_sw128(k_addr + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(&s_full[s]);
+        tc::mma_commit(&k_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nblk > 1) ok = issue_s(1);
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&p_full[s], (uint32_t)((j >> 1) & 1), p.err) ||
+            !tc::mbar_wait(&v_full[s], (uint32_t)((j >> 1) & 1), p.err)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t p_addr = tc::smem_u32(smem + C::OFF_P + s * C::P_BYTES);
+        const uint32_t v_addr = tc::smem_u32(smem + C::OFF_V + s * C::V_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BKV / 16; ++k) {
+          const uint64_t ad = tc::sdesc_sw128(p_addr + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sdesc_sw128(v_addr + k * 2048, C::BKV * 128, 1024);
+          tc::mma_f16_ss(t_o, ad, bd, IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(o_upd);
+        tc::mma_commit(&v_empty[s]);
+        if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + epilogue: warps 2..5, thread = query row ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // row inside the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j & 1;
+      if (!tc::mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1), p.err) || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      uint32_t sr[128];
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tbase + s * 128 + c * 32 + lane_off, sr + c * 32);
+      tc::tmem_wait_ld();
+      const int valid = (int)(p.Sk - (int64_t)j * C::BKV < C::BKV ? p.Sk - (int64_t)j * C::BKV : C::BKV);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c)
+        if (c < valid) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      const float m_blk = mx * p.scale_log2;
+      // lazy rescale: keep the old max unless the new one is more than 2^8 larger
+      const bool need = (m == -INFINITY) || (m_blk > m + 8.f);
+      float alpha = 1.f;
+      if (need) {
+        const float m_new = fmaxf(m, m_blk);
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+        m = m_new;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O holds the sum up to PV_{j-1}; wait for it, then scale this warp's rows in TMEM
+        if (!tc::mbar_wait(o_upd, (uint32_t)((j - 1) & 1), p.err)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t orow[32];
+          tc::tmem_ld32(t_o + c * 32 + lane_off, orow);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
+          tc::tmem_st16(t_o + c * 32 + lane_off, orow);
+          tc::tmem_st16(t_o + c * 32 + 16 + lane_off, orow + 16);
+        }
+        tc::tmem_wait_st();
+      }
+      l *= alpha;
+      // P = exp2(s * scale_log2 - m), written as bf16 into the swizzled A tile of the PV MMA
+      uint8_t* ptile = smem + C::OFF_P + s * C::P_BYTES;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {  // 16 granules of 8 keys
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c0 = g * 8 + 2 * e;
+          float p0 = c0 < valid ? ex2(__uint_as_float(sr[c0]) * p.scale_log2 - m) : 0.f;
+          float p1 = c0 + 1 < valid ? ex2(__uint_as_float(sr[c0 + 1]) * p.scale_log2 - m) : 0.f;
+          rowsum += p0 + p1;
+          w[e] = pack2(p0, p1, BF16);
+        }
+        uint8_t* row = ptile + (g >> 3) * (128 * 128) + r * 128;
+        *reinterpret_cast<uint4*>(row + (((g & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += rowsum;
+      tc::fence_async_shared();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&p_full[s]);
+    }
+    // ---------------- epilogue: O / l -> global, lse ----------------
+    if (ok && tc::mbar_wait(o_upd, (uint32_t)((nblk - 1) & 1), p.err)) {
+      tc::tc_fence_after();
+      const int64_t qrow = q0 + r;
+      const float inv = 1.f / l;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = (T*)p.o + (int64_t)b * p.o_s[0] + (int64_t)h * p.o_s[1] + qrow * p.o_s[2];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        __syncwarp();
+        tc::tmem_ld32(t_o + c * 32 + lane_off, ov);
+        tc::tmem_wait_ld();
+        if (qrow < p.Sq) {
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            w[e] = pack2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv, BF16);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        }
+      }
+      if (qrow < p.Sq) p.lse[(int64_t)bh * p.Sq + qrow] = (m + __log2f(l)) * 0.6931471805599453f;
+    } else {
+      *abort_flag = 1;
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+}
+
+// ---- tensor maps over [B, H, S, D] with arbitrary (b, h, s) strides -----------------------------
+bool make_bhsd_map(CUtensorMap* m, const void* base, const int64_t* s3, int64_t B, int64_t H, int64_t S, int64_t D,
+                   bool bf16, uint32_t box_rows) {
+  uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  uint64_t strides[3] = {(uint64_t)s3[2] * 2, (uint64_t)s3[1] * 2, (uint64_t)s3[0] * 2};
+  // size-1 dims: any valid stride
+  if (S == 1) strides[0] = (uint64_t)D * 2;
+  if (H == 1) strides[1] = strides[0] * (uint64_t)S;
+  if (B == 1) strides[2] = strides[1] * (uint64_t)H;
+  uint32_t box[4] = {64, box_rows, 1, 1};
+  return make_tmap(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims,
+                   strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+bool strides_ok(const int64_t* s3, int64_t B, int64_t H, int64_t S) {
+  auto ok = [](int64_t v) { return v > 0 && (v * 2) % 16 == 0; };
+  return (S == 1 || ok(s3[2])) && (H == 1 || ok(s3[1])) && (B == 1 || ok(s3[0]));
+}
+
+}  // namespace
+
+bool attn_tc_eligible(const b2_attn_args* a) {
+  if (a->dtype != B2_BF16 && a->dtype != B2_F16) return false;
+  if (a->D != 64 && a->D != 128) return false;
+  if (!device_info().tcgen05) return false;
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (!al(a->q) || !al(a->k) || !al(a->v) || !al(a->o)) return false;
+  if (!strides_ok(a->q_s, a->B, a->H, a->Sq) || !strides_ok(a->k_s, a->B, a->H, a->Sk) ||
+      !strides_ok(a->v_s, a->B, a->H, a->Sk))
+    return false;
+  if ((a->o_s[2] % 8) || (a->o_s[1] % 8) || (a->o_s[0] % 8)) return false;  // 16-byte vector stores of O rows
+  if (a->Sq >= (1ll << 31) || a->Sk >= (1ll << 31) || a->B * a->H > 65535) return false;
+  return true;
+}
+
+template <int D, bool BF16>
+int launch_fwd(const b2_attn_args* a, cudaStream_t st) {
+  using C = FwdCfg<D>;
+  static bool attr = false;
+  if (!attr) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(attn_fwd_tc<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                            "attn_fwd_tc attr"))
+      return rc;
+    attr = true;
+  }
+  CUtensorMap tq, tk, tv;
+  if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, D, BF16, 128) ||
+      !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, D, BF16, 128) ||
+      !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, D, BF16, 128))
+    return fail(B2_ERR_ARG, "attn_tc: tensor map rejected");
+  AttnTcParams p{};
+  p.B = a->B, p.H = a->H, p.Sq = a->Sq, p.Sk = a->Sk;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.o = a->o;
+  for (int i = 0; i < 3; ++i) p.o_s[i] = a->o_s[i];
+  p.lse = a->lse;
+  p.err = device_error_ptr();
+  dim3 grid((unsigned)((a->Sq + 127) / 128), (unsigned)(a->B * a->H));
+  LaunchScope ls("attn_fwd_tc", st);
+  attn_fwd_tc<D, BF16><<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, p);
+  return after_launch("attn_fwd_tc");
+}
+
+int attn_tc_fwd(const b2_attn_args* a, cudaStream_t st) {
+  const bool bf16 = a->dtype == B2_BF16;
+  if (a->D == 128) return bf16 ? launch_fwd<128, true>(a, st) : launch_fwd<128, false>(a, st);
+  return bf16 ? launch_fwd<64, true>(a, st) : launch_fwd<64, false>(a, st);
+}
+
+int attn_simt_bwd_dispatch(const b2_attn_args* a, cudaStream_t st);  // attn_simt.cu
+
+namespace {
+
+// ==================================================================================================
+// backward (D = 128): one CTA per (128-key tile, batch*head), walking 64-query tiles
+// ==================================================================================================
+struct BwdCfg {
+  static constexpr int D = 128, BKV = 128, BQ = 64;
+  static constexpr int KV_BYTES = BKV * D * 2;        // K or V tile, 32 KB
+  static constexpr int QT_BYTES = BQ * D * 2;         // Q or dO tile, 16 KB
+  static constexpr int PT_BYTES = BKV * BQ * 2;       // P^T or dS^T tile, 16 KB
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KV_BYTES;
+  static constexpr int OFF_Q = OFF_V + KV_BYTES;      // 2 stages
+  static constexpr int OFF_DO = OFF_Q + 2 * QT_BYTES; // 2 stages
+  static constexpr int OFF_P = OFF_DO + 2 * QT_BYTES; // 2 buffers
+  static constexpr int OFF_DS = OFF_P + 2 * PT_BYTES; // 2 buffers
+  static constexpr int OFF_BAR = OFF_DS + 2 * PT_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int THREADS = 192;
+  // TMEM columns: S^T [0,64) dP^T [64,128) dQ^T [128,192) dV [256,384) dK [384,512)
+  static constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_DV = 256, T_DK = 384, TMEM_COLS = 512;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       AttnTcParams p, int bf16_flag) {
+  using C = BwdCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* kv_full = bar + 0;
+  uint64_t* q_full = bar + 1;     // [2] Q_i + dO_i landed
+  uint64_t* q_empty = bar + 3;    // [2] all MMAs reading Q_i / dO_i done
+  uint64_t* sdp_full = bar + 5;   // S^T_i and dP^T_i in TMEM
+  uint64_t* pds_full = bar + 6;   // [2] P^T_i / dS^T_i written (count 128)
+  uint64_t* pds_empty = bar + 8;  // [2] MMAs reading P^T_i / dS^T_i done
+  uint64_t* dq_full = bar + 10;   // dQ^T_i in TMEM
+  uint64_t* dq_empty = bar + 11;  // dQ^T_i drained (count 128)
+  uint64_t* dkv_full = bar + 12;  // final dK, dV in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 14);
+  const bool BF16 = bf16_flag != 0;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k0 = blockIdx.x * C::BKV;
+  const int bh = blockIdx.y;
+  const int b = bh / (int)p.H, h = bh % (int)p.H;
+  const int ntile = (int)((p.Sq + C::BQ - 1) / C::BQ);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&q_full[i], 1);
+      tc::mbar_init(&q_empty[i], 1);
+      tc::mbar_init(&pds_full[i], 128);
+      tc::mbar_init(&pds_empty[i], 1);
+    }
+    tc::mbar_init(sdp_full, 1);
+    tc::mbar_init(dq_full, 1);
+    tc::mbar_init(dq_empty, 128);
+    tc::mbar_init(dkv_full, 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer: K, V once; Q_i, dO_i into a 2-stage ring ----------------
+      tc::mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
+      for (int c = 0; c < 2; ++c) {
+        tc::tma_load_4d(smem + C::OFF_K + c * (C::BKV * 128), &tmK, kv_full, c * 64, k0, h, b);
+        tc::tma_load_4d(smem + C::OFF_V + c * (C::BKV * 128), &tmV, kv_full, c * 64, k0, h, b);
+      }
+      int issued[2] = {0, 0};
+      bool ok = true;
+      for (int i = 0; i < ntile; ++i) {
+        const int s = i & 1;
+        if (!tc::mbar_wait(&q_empty[s], ((uint32_t)(i >> 1) & 1) ^ 1, p.err) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        tc::mbar_arrive_expect_tx(&q_full[s], 2 * C::QT_BYTES);
+        for (int c = 0; c < 2; ++c) {
+          tc::tma_load_4d(smem + C::OFF_Q + s * C::QT_BYTES + c * (C::BQ * 128), &tmQ, &q_full[s], c * 64, i * C::BQ, h, b);
+          tc::tma_load_4d(smem + C::OFF_DO + s * C::QT_BYTES + c * (C::BQ * 128), &tmDO, &q_full[s], c * 64, i * C::BQ, h, b);
+        }
+        issued[s]++;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        tc::mbar_wait(kv_full, 0, nullptr);
+        for (int s = 0; s < 2; ++s)
+          if (issued[s]) tc::mbar_wait(&q_full[s], (uint32_t)((issued[s] - 1) & 1), nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t IDESC_SDP = tc::idesc_f16(128, C::BQ, BF16, false, false);  // K Q^T, V dO^T: both K-major
+      const uint32_t IDESC_KV = tc::idesc_f16(128, C::D, BF16, false, true);     // P^T dO, dS^T Q: B MN-major
+      const uint32_t IDESC_DQ = tc::idesc_f16(128, C::BQ, BF16, true, true);     // K^T dS^T: A and B MN-major
+      const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K), v_addr = tc::smem_u32(smem + C::OFF_V);
+      bool ok = tc::mbar_wait(kv_full, 0, p.err);
+      auto issue_sdp = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!tc::mbar_wait(&q_full[s], (uint32_t)((i >> 1) & 1), p.err)) return false;
+        tc::tc_fence_after();
+        const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES);
+        const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::D / 16; ++k) {
+          const uint32_t ka = (k >> 2) * (C::BKV * 128) + (k & 3) * 32;
+          const uint32_t qa = (k >> 2) * (C::BQ * 128) + (k & 3) * 32;
+          tc::mma_f16_ss(tbase + C::T_S, tc::sdesc_sw128(k_addr + ka, 16, 1024), tc::sdesc_sw128(q_addr + qa, 16, 1024),
+                         IDESC_SDP, k > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < C::D / 16; ++k) {
+          const uint32_t ka = (k >> 2) * (C::BKV * 128) + (k & 3) * 32;
+          const uint32_t qa = (k >> 2) * (C::BQ * 128) + (k & 3) * 32;
+          tc::mma_f16_ss(tbase + C::T_DP, tc::sdesc_sw128(v_addr + ka, 16, 1024), tc::sdesc_sw128(do_addr + qa, 16, 1024),
+                         IDESC_SDP, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(sdp_full);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int i = 0; i < ntile && ok; ++i) {
+        const int s = i & 1;
+        const uint32_t ph = (uint32_t)((i >> 1) & 1);
+        if (!tc::mbar_wait(&pds_full[s], ph, p.err)) { ok = false; break; }
+        tc::tc_fence_after();
+        // the softmax threads have read S^T_i / dP^T_i: the next tile's scores can go into TMEM now
+        if (i + 1 < ntile && !issue_sdp(i + 1)) { ok = false; break; }
+        const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES);
+        const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES);
+        const uint32_t pt_addr = tc::smem_u32(smem + C::OFF_P + s * C::PT_BYTES);
+        const uint32_t ds_addr = tc::smem_u32(smem + C::OFF_DS + s * C::PT_BYTES);
+        // dV += P^T dO ; dK += dS^T Q   (M = 128 keys, N = D, K = 64 queries)
+#pragma unroll
+        for (int k = 0; k < C::BQ / 16; ++k) {
+          tc::mma_f16_ss(tbase + C::T_DV, tc::sdesc_sw128(pt_addr + k * 32, 16, 1024),
+                         tc::sdesc_sw128(do_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < C::BQ / 16; ++k) {
+          tc::mma_f16_ss(tbase + C::T_DK, tc::sdesc_sw128(ds_addr + k * 32, 16, 1024),
+                         tc::sdesc_sw128(q_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&q_empty[s]);
+        // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
+        if (i > 0 && !tc::mbar_wait(dq_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
+        tc::tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < C::BKV / 16; ++k) {
+          tc::mma_f16_ss(tbase + C::T_DQ, tc::sdesc_sw128(k_addr + k * 2048, C::BKV * 128, 1024),
+                         tc::sdesc_sw128(ds_addr + k * 2048, 8192, 1024), IDESC_DQ, k > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(dq_full);
+        tc::mma_commit(&pds_empty[s]);
+      }
+      if (ok) tc::mma_commit(dkv_full);
+      else *abort_flag = 1;
+    }
+  } else {
+    // ---------------- warps 2..5: P^T / dS^T (thread = key row), dQ drain, dK/dV epilogue -----------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // key row within the tile == TMEM lane (also d for dQ^T)
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float LOG2E = 1.4426950408889634f;
+    bool ok = true;
+    auto drain_dq = [&](int i) -> bool {
+      if (!tc::mbar_wait(dq_full, (uint32_t)(i & 1), p.err)) return false;
+      tc::tc_fence_after();
+      uint32_t v[64];
+      __syncwarp();
+      tc::tmem_ld32(tbase + C::T_DQ + lane_off, v);
+      tc::tmem_ld32(tbase + C::T_DQ + 32 + lane_off, v + 32);
+      tc::tmem_wait_ld();
+      tc::tc_fence_before();
+      tc::mbar_arrive(dq_empty);
+      // dq_acc layout [bh][d][Sq_pad]: thread d adds 64 consecutive queries
+      const int64_t sq_pad = (p.Sq + 63) / 64 * 64;
+      float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * C::D + r) * sq_pad + (int64_t)i * C::BQ);
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]) * p.scale, __uint_as_float(v[4 * e + 1]) * p.scale,
+                                       __uint_as_float(v[4 * e + 2]) * p.scale, __uint_as_float(v[4 * e + 3]) * p.scale));
+      return true;
+    };
+    for (int i = 0; i < ntile; ++i) {
+      const int s = i & 1;
+      if (!tc::mbar_wait(sdp_full, (uint32_t)(i & 1), p.err) || *abort_flag) { ok = false; break; }
+      tc::tc_fence_after();
+      uint32_t sv[64], dp[64];
+      __syncwarp();
+      tc::tmem_ld32(tbase + C::T_S + lane_off, sv);
+      tc::tmem_ld32(tbase + C::T_S + 32 + lane_off, sv + 32);
+      tc::tmem_ld32(tbase + C::T_DP + lane_off, dp);
+      tc::tmem_ld32(tbase + C::T_DP + 32 + lane_off, dp + 32);
+      tc::tmem_wait_ld();
+      // P^T / dS^T buffer s was last read by the MMAs of tile i-2
+      if (i >= 2 && !tc::mbar_wait(&pds_empty[s], (uint32_t)(((i - 2) >> 1) & 1), p.err)) { ok = false; break; }
+      const int64_t qbase = (int64_t)i * C::BQ;
+      const float* lse_row = p.lse + (int64_t)bh * p.Sq;
+      const float* dl_row = p.delta + (int64_t)bh * p.Sq;
+      uint8_t* pt = smem + C::OFF_P + s * C::PT_BYTES + r * 128;
+      uint8_t* dst = smem + C::OFF_DS + s * C::PT_BYTES + r * 128;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        uint32_t wp[4], wd[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int c = g * 8 + 2 * e + t;
+            const int64_t qi = qbase + c;
+            float L = qi < p.Sq ? __ldg(lse_row + qi) * LOG2E : INFINITY;
+            float dl = qi < p.Sq ? __ldg(dl_row + qi) : 0.f;
+            float pp = ex2(__uint_as_float(sv[c]) * p.scale_log2 - L);
+            pv[t] = pp;
+            dv[t] = pp * (__uint_as_float(dp[c]) - dl);
+          }
+          wp[e] = pack2(pv[0], pv[1], BF16);
+          wd[e] = pack2(dv[0], dv[1], BF16);
+        }
+        const int off = ((g ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(pt + off) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
+        *reinterpret_cast<uint4*>(dst + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      tc::fence_async_shared();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&pds_full[s]);
+      if (i > 0 && !drain_dq(i - 1)) { ok = false; break; }
+    }
+    if (ok && ntile > 0) ok = drain_dq(ntile - 1);
+    // ---------------- dK, dV epilogue ----------------
+    if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
+      tc::tc_fence_after();
+      const int64_t krow = k0 + r;
+      using Tb = __nv_bfloat16;
+      for (int which = 0; which < 2; ++which) {  // 0: dV, 1: dK (times scale)
+        void* base = which ? p.dk : p.dv;
+        const int64_t* st = which ? p.dk_s : p.dv_s;
+        const float mul = which ? p.scale : 1.f;
+        const uint32_t tcol = which ? C::T_DK : C::T_DV;
+#pragma unroll
+        for (int c = 0; c < C::D / 32; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tc::tmem_ld32(tbase + tcol + c * 32 + lane_off, v);
+          tc::tmem_wait_ld();
+          if (base && krow < p.Sk) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              w[e] = pack2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul, BF16);
+            uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<Tb*>(base) + (int64_t)b * st[0] + (int64_t)h * st[1] +
+                                                 krow * st[2] + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          }
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+}
+
+// dq[b,h,q,d] = dq_acc[bh][d][q] (fp32 -> T), 32x32 tiles transposed through shared memory.
+template <typename T>
+__global__ void dq_convert(const float* __restrict__ acc, T* __restrict__ dq, int64_t H, int64_t Sq, int64_t sq_pad,
+                           int64_t D, int64_t s0, int64_t s1, int64_t s2) {
+  __shared__ float tile[32][33];
+  const int64_t bh = blockIdx.z, b = bh / H, h = bh % H;
+  const int64_t q0 = (int64_t)blockIdx.x * 32, d0 = (int64_t)blockIdx.y * 32;
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    int64_t d = d0 + y, q = q0 + threadIdx.x;
+    tile[y][threadIdx.x] = (d < D && q < Sq) ? acc[(bh * D + d) * sq_pad + q] : 0.f;
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    int64_t q = q0 + y, d = d0 + threadIdx.x;
+    if (q < Sq && d < D) dq[b * s0 + h * s1 + q * s2 + d] = from_f32<T>(tile[threadIdx.x][y]);
+  }
+}
+
+}  // namespace
+
+bool attn_tc_bwd_eligible(const b2_attn_args* a) {
+  if (!attn_tc_eligible(a) || a->D != 128 || a->dtype != B2_BF16) return false;
+  if (!strides_ok(a->do_s, a->B, a->H, a->Sq) || ((uintptr_t)a->d_o & 15)) return false;
+  auto al = [](const void* p) { return p == nullptr || ((uintptr_t)p & 15) == 0; };
+  if (!al(a->dk) || !al(a->dv)) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((a->dk && a->dk_s[i] % 8) || (a->dv && a->dv_s[i] % 8)) return false;
+  return true;
+}
+
+uint64_t attn_bwd_ws_bytes(const b2_attn_args* a) {
+  if (!attn_tc_bwd_eligible(a)) return 0;
+  const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
+  return (uint64_t)(a->B * a->H) * (uint64_t)a->D * (uint64_t)sq_pad * 4;
+}
+
+int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
+  if (!attn_tc_bwd_eligible(a)) return attn_simt_bwd_dispatch(a, st);
+  if (!a->workspace) return fail(B2_ERR_ARG, "attn_bwd: workspace of b2_attn_bwd_workspace_bytes() required");
+  using C = BwdCfg;
+  static bool attr = false;
+  if (!attr) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+                            "attn_bwd_tc attr"))
+      return rc;
+    attr = true;
+  }
+  if (int rc = attn_delta_launch(a, st)) return rc;
+  const uint64_t ws = attn_bwd_ws_bytes(a);
+  if (int rc = check_cuda(cudaMemsetAsync(a->workspace, 0, ws, st), "attn_bwd: clear dQ accumulator")) return rc;
+  CUtensorMap tq, tk, tv, tdo;
+  if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, 128, true, 64) ||
+      !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, 128, true, 128) ||
+      !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, 128, true, 128) ||
+      !make_bhsd_map(&tdo, a->d_o, a->do_s, a->B, a->H, a->Sq, 128, true, 64))
+    return fail(B2_ERR_ARG, "attn_bwd_tc: tensor map rejected");
+  AttnTcParams p{};
+  p.B = a->B, p.H = a->H, p.Sq = a->Sq, p.Sk = a->Sk;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.lse = a->lse;
+  p.delta = a->delta;
+  p.dq_acc = (float*)a->workspace;
+  p.dk = a->dk, p.dv = a->dv;
+  for (int i = 0; i < 3; ++i) p.dk_s[i] = a->dk_s[i], p.dv_s[i] = a->dv_s[i];
+  p.err = device_error_ptr();
+  {
+    dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)(a->B * a->H));
+    LaunchScope ls("attn_bwd_tc", st);
+    attn_bwd_tc_kernel<<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, tdo, p, 1);
+    if (int rc = after_launch("attn_bwd_tc")) return rc;
+  }
+  if (a->dq) {
+    const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
+    dim3 grid((unsigned)((a->Sq + 31) / 32), (unsigned)((a->D + 31) / 32), (unsigned)(a->B * a->H));
+    LaunchScope ls("attn_dq_convert", st);
+    dq_convert<__nv_bfloat16><<<grid, dim3(32, 8), 0, st>>>((const float*)a->workspace, (__nv_bfloat16*)a->dq, a->H,
+                                                            a->Sq, sq_pad, a->D, a->dq_s[0], a->dq_s[1], a->dq_s[2]);
+    if (int rc = after_launch("attn_dq_convert")) return rc;
+  }
+  return 0;
+}
+
 }  // namespace b2
 
-extern "C" uint64_t b2_attn_bwd_workspace_bytes(const b2_attn_args*) { return 0; }
+extern "C" uint64_t b2_attn_bwd_workspace_bytes(const b2_attn_args* a) { return a ? b2::attn_bwd_ws_bytes(a) : 0; }

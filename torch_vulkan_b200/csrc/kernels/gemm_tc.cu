@@ -45,14 +45,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Encodes a 2-D or 3-D tiled tensor map. dims/strides: innermost first; strides in bytes for dims
+// Encodes a 1..5-D tiled tensor map. dims/strides: innermost first; strides in bytes for dims
 // 1.. (dim 0 is contiguous). Returns false if the driver rejects it.
 bool make_tmap(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw) {
   EncodeTiledFn f = encode_fn();
   if (!f) return false;
-  cuuint64_t gd[3], gs[2];
-  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  if (rank < 1 || rank > 5) return false;
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5] = {1, 1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     gd[i] = dims[i];
     bx[i] = box[i];
