@@ -1,0 +1,459 @@
+"""Benchmark of the hot path on B200 (the driver's contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the configuration its metric is quoted on): fused scaled-dot-product
+attention forward + backward, bf16, B=1, H=16, S_q=S_kv=1024, D=128, q/k/v/dO ~ N(0,1), scale 1/sqrt(128),
+no mask, no dropout. A "step" is one forward + backward pass (O, logsumexp, dQ, dK, dV) through the public
+API (torch.nn.functional.scaled_dot_product_attention + autograd on CUDA tensors, served by this package's
+tcgen05 kernels). FLOPs per step = 4*B*H*S^2*D*(1 + 2.5) = 30.06 GFLOP (tools/bench_attention.py:39 of the
+reference).
+
+* value  — whole-job TFLOP/s with inputs resident in HBM: each timed step is bracketed by CUDA events on the
+           compute stream; the L2 is flushed (a 256 MiB buffer is rewritten) between timed steps, outside the
+           events; value = N * FLOPs / (max over ranks of the mean step time).
+* e2e    — the same metric through the same public call with HOST inputs: every step copies q/k/v/dO from
+           pinned host memory, runs forward + backward and copies O/dQ/dK/dV back, all inside the timed region.
+* roofline — dominant kernel of the step (by the library's per-launch CUDA-event profile, measured in a
+           separate pass): algorithmic FLOPs per launch / mean launch time vs the measured bf16 peak.
+* cpu_baseline — the reference's CPU path (stock PyTorch CPU SDPA, what torch-vulkan's CPU fallback runs),
+           timed on this host's cores in bf16 over a bounded sample (rank 0, N=1).
+* extra  — the other two BASELINE metrics measured the same way: the int8-dequant GEMM and the
+           row kernels.
+
+Multi-GPU (torchrun, one process per GPU): attention does not shard, so each rank runs an independent
+replica of the step ("replicas only", weak scaling); the barrier + max-over-ranks timing applies.
+`--impl reference` times the reference's CPU implementation (torch CPU ATen) of the same workload on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+import torch.nn.functional as F  # noqa: E402
+
+B, H, S, D = 1, 16, 1024, 128
+FWD_FLOPS = 4.0 * B * H * S * S * D
+STEP_FLOPS = FWD_FLOPS * 3.5  # fwd + bwd (2.5x)
+METRIC = "attn fwd+bwd TFLOP/s"
+CONFIG = {"workload": "fused SDPA fwd+bwd (BASELINE configs[1])", "batch": B, "heads": H, "seq_q": S, "seq_kv": S,
+          "head_dim": D, "scale": "1/sqrt(128)", "mask": None, "dropout": 0.0, "l2": "flushed between timed steps (256 MiB rewrite)"}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic(name):
+    """Per-launch DRAM bytes of kernel `name` from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == name:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+def make_inputs(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(B, H, S, D, generator=g).to(torch.bfloat16) for _ in range(4)]
+
+
+# ---------------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.idx = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5:
+            time.sleep(0.01)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def mark(self):
+        return len(self.lines)
+
+    def stop(self, since=0):
+        if self.proc is None:
+            return None
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [l.split(", ") for l in self.lines[max(0, since - 1):] if l]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch_vulkan_b200 as tv
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    qh, kh, vh, doh = make_inputs(seed=rank)
+    q, k, v = (t.to(dev).requires_grad_(True) for t in (qh, kh, vh))
+    do = doh.to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step(q=q, k=k, v=v):
+        o = F.scaled_dot_product_attention(q, k, v)
+        return (o,) + torch.autograd.grad(o, (q, k, v), do)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    tv.reset_counts()
+    o = step()
+    torch.cuda.synchronize()
+    kc = tv.kernel_counts()
+    assert kc.get("aten::_scaled_dot_product_fused_attention_overrideable", 0) == 1, kc
+
+    # eager per-step time (host launch overhead included), reported for transparency
+    K = args.steps
+    ke0, ke1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ke0.record(stream)
+    for _ in range(min(K, 50)):
+        step()
+    ke1.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = ke0.elapsed_time(ke1) / min(K, 50)
+
+    # the step as a CUDA graph: the same public calls (sdpa forward + autograd backward), captured once
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        # fresh leaves whose autograd nodes belong to the capture stream
+        qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+        for _ in range(2):
+            step(qg, kg, vg)
+    stream.wait_stream(side)
+    launches_before = tv.stats()["launches"]
+    with torch.cuda.graph(graph):
+        outs_g = step(qg, kg, vg)
+    launches_per_step = tv.stats()["launches"] - launches_before  # this library's kernels in the graph
+    graph.replay()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+    mark = sampler.mark()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.zero_()  # rewrite > L2 between timed steps (outside the events)
+        starts[i].record(stream)
+        graph.replay()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = launches_per_step * K
+    clocks = sampler.stop(mark) if rank == 0 else None
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / K
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = t.item()
+    value = world * STEP_FLOPS / (ms_max * 1e-3) / 1e12
+    del graph
+
+    # ---- e2e through the same public call with host buffers --------------------------------------
+    pin = [x.pin_memory() for x in (qh, kh, vh, doh)]
+    outs = [torch.empty(B, H, S, D, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+
+    def e2e_step():
+        qd, kd, vd = (x.to(dev, non_blocking=True).requires_grad_(True) for x in pin[:3])
+        dod = pin[3].to(dev, non_blocking=True)
+        od = F.scaled_dot_product_attention(qd, kd, vd)
+        grads = torch.autograd.grad(od, (qd, kd, vd), dod)
+        for dst, src in zip(outs, (od.detach(),) + grads):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    ke = max(10, min(K, 200))
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(ke):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / ke], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = {"value": world * STEP_FLOPS / (te.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": 4 * B * H * S * D * 2, "d2h_bytes_per_step": 4 * B * H * S * D * 2,
+           "ms_per_step": te.item()}
+
+    # ---- per-kernel profile (separate pass): dominant kernel and its roofline -----------------------
+    peaks = load_peaks()
+    tv.profile_enable(True)
+    tv.profile()  # drain earlier records
+    torch.cuda.synchronize()
+    tv.gpu_sleep(100_000_000)  # hold the stream so the profiled launches run back to back
+    for _ in range(20):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    rows = [r.split("\t") for r in tv.profile().splitlines() if r]
+    tv.profile_enable(False)
+    prof = {r[0]: (float(r[1]), int(r[2])) for r in rows}
+    kernel_flops = {"attn_bwd_tc": 2.5 * FWD_FLOPS, "attn_fwd_tc": FWD_FLOPS}
+    dom = max((n for n in prof if n in kernel_flops), key=lambda n: prof[n][0], default=None)
+    roofline = None
+    if dom:
+        per_launch_ms = prof[dom][0] / prof[dom][1]
+        achieved = kernel_flops[dom] / (per_launch_ms * 1e-3) / 1e12
+        traffic = load_traffic(dom)
+        roofline = {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": traffic,
+                    "peak_source": peaks["source"] + " (burst bf16 cuBLAS)",
+                    "launch_ms": round(per_launch_ms, 5),
+                    "kernels_ms_per_step": {n: round(v[0] / v[1], 5) for n, v in prof.items()}}
+
+    extra = None
+    if rank == 0 and not args.no_extra:
+        extra = run_extra(tv, dev, flush, peaks)
+
+    result = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+              "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max, 5), "higher_is_better": True,
+              "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+              "config": dict(CONFIG, parallelism=f"replicas x{world}" if world > 1 else "single GPU"),
+              "e2e": e2e, "gpu_launches": launches, "gpu_launches_per_step": launches_per_step,
+              "eager_ms_per_step": round(eager_ms, 5), "timing": "CUDA-graph replay of the public-API step",
+              "roofline": roofline, "clocks": clocks}
+    if extra:
+        result["extra"] = extra
+    return result
+
+
+def timed(fn, flush, iters=50, warm=5):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / iters
+
+
+def run_extra(tv, dev, flush, peaks):
+    """configs[0] int8-dequant linear (x[1024,2048] @ (W int8 [6144,2048] * per-row fp32 scale)^T + bias)
+    and configs[2] row kernels, each with its own roofline fraction."""
+    out = {}
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+    qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8).to(dev)
+    s = (torch.rand(6144, generator=g) * 9e-3 + 1e-3).to(dev)
+    bias = (torch.randn(6144, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    ms = timed(lambda: tv.int8_linear(x, qw, s, bias), flush)
+    fl = 2.0 * 1024 * 6144 * 2048
+    out["int8_gemm"] = {"metric": "int8-deq GEMM TFLOP/s", "config": "BASELINE configs[0] (M1024 N6144 K2048, per-row fp32 scale, bias)",
+                        "value": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 5),
+                        "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
+    xs = (torch.randn(16, 1024, 1024, generator=g) * 2).to(torch.bfloat16).to(dev).requires_grad_(True)
+    gs = torch.randn(16, 1024, 1024, generator=g).to(torch.bfloat16).to(dev)
+    ys = torch.softmax(xs, -1)
+    ms_f = timed(lambda: torch.softmax(xs, -1), flush)
+    ms_b = timed(lambda: torch.ops.aten._softmax_backward_data(gs, ys, -1, torch.bfloat16), flush)
+    xl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+    wl = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
+    bl = (0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
+    gl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+    yl, mu, rs = torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6)
+    ms_lf = timed(lambda: torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6), flush)
+    ms_lb = timed(lambda: torch.ops.aten.native_layer_norm_backward(gl, xl, (2048,), mu, rs, wl, bl, [True, True, True]), flush)
+    hbm = peaks["hbm_gbs"]
+
+    def gbs(nbytes, ms_):
+        return round(nbytes / (ms_ * 1e-3) / 1e9, 1)
+
+    out["rows"] = {"metric": "row kernels GB/s (algorithmic bytes)", "config": "BASELINE configs[2]", "peak_gbs": hbm,
+                   "softmax_fwd": gbs(67.1e6, ms_f), "softmax_bwd": gbs(100.7e6, ms_b),
+                   "layernorm_fwd": gbs(8.40e6, ms_lf), "layernorm_bwd": gbs(12.6e6, ms_lb)}
+    for k2 in ("softmax_fwd", "softmax_bwd", "layernorm_fwd", "layernorm_bwd"):
+        out["rows"][k2 + "_frac"] = round(out["rows"][k2] / hbm, 4)
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference's CPU path (stock PyTorch CPU SDPA) on the host cores
+# ---------------------------------------------------------------------------------------------------
+def cpu_sdpa_sample(heads, reps=1):
+    """fwd + bwd of `heads` heads of config 2 on the CPU in bf16; returns (seconds, flops)."""
+    qh, kh, vh, doh = make_inputs(seed=123)
+    q, k, v, do = (t[:, :heads].contiguous() for t in (qh, kh, vh, doh))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        qc, kc, vc = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = F.scaled_dot_product_attention(qc, kc, vc)
+        o.backward(do)
+    dt = time.perf_counter() - t0
+    return dt, reps * STEP_FLOPS * heads / H
+
+
+def cpu_baseline(budget_s=12.0):
+    """About `budget_s` seconds of the reference's CPU path on all host threads."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cpu_sdpa_sample(H)  # warm-up
+    dt1, _ = cpu_sdpa_sample(H)
+    reps = int(max(1, min(1000, budget_s / max(dt1, 1e-4))))
+    dt, fl = cpu_sdpa_sample(H, reps)
+    return {"value": round(fl / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full configs[1] fwd+bwd passes (torch CPU SDPA, bf16) in {dt:.1f} s",
+            "cpu": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cpu_sdpa_sample(1)
+    dt1, _ = cpu_sdpa_sample(1)
+    # each step is a bounded sample (a subset of heads) so that warmup + steps end within ~2 minutes
+    per_step_budget = 100.0 / max(1, args.steps + args.warmup)
+    heads = int(max(1, min(H, per_step_budget / max(dt1, 1e-3))))
+    for _ in range(args.warmup):
+        cpu_sdpa_sample(heads)
+    tot_t, tot_f = 0.0, 0.0
+    for _ in range(args.steps):
+        dt, fl = cpu_sdpa_sample(heads)
+        tot_t += dt
+        tot_f += fl
+    value = tot_f / tot_t / 1e12
+    ms = tot_t / args.steps * 1e3
+    sample = f"{heads} of {H} heads of configs[1] fwd+bwd per step (torch CPU SDPA math, bf16)"
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": dict(CONFIG, parallelism="host CPU"),
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": sample, "cpu": _cpu_model()},
+            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    res = run_ours(args, rank, world, local_rank)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

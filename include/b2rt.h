@@ -133,6 +133,10 @@ void b2rt_reset_op_counts(void);
  * Format "name\tms\tcount\n", sorted by time. */
 void b2rt_profile_enable(int on);
 size_t b2rt_profile_dump(char* buf, size_t cap);
+/* Occupies `stream` for `ns` nanoseconds (<= 1 s) with a one-thread spin on the global timer, so a
+ * host can enqueue work behind it and have the GPU run that work back to back (measurement aid;
+ * no counterpart in the reference). */
+int b2rt_gpu_sleep(uint64_t ns, b2_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Kernel entry points                                                                         */

@@ -211,6 +211,15 @@ def profile_enable(on: bool = True) -> None:
     _lib.b2rt_profile_enable(1 if on else 0)
 
 
+def gpu_sleep(ns: int, stream=None) -> None:
+    """Occupy the (current) CUDA stream for `ns` nanoseconds (<= 1 s); work enqueued behind it then runs
+    back to back without host launch gaps."""
+    s = stream if stream is not None else torch.cuda.current_stream()
+    rc = _lib.b2rt_gpu_sleep(ctypes.c_uint64(int(ns)), ctypes.c_void_p(s.cuda_stream))
+    if rc != 0:
+        raise RuntimeError("gpu_sleep: " + last_error())
+
+
 def profile() -> str:
     """'name\\tms\\tcount' lines of per-kernel GPU time (after profile_enable or B2RT_PROFILE=1)."""
     return _text(_lib.b2rt_profile_dump)

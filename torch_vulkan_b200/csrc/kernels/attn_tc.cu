@@ -72,28 +72,30 @@ struct AttnTcParams {
 };
 
 // ==================================================================================================
-// forward
+// forward: two softmax warpgroups split the KV blocks (even / odd), each with its own TMEM S and O
 // ==================================================================================================
 template <int D>
 struct FwdCfg {
   static constexpr int BQ = 128, BKV = 128;
   static constexpr int DCH = D / 64;                 // 64-element chunks along D
-  static constexpr int Q_BYTES = BQ * D * 2;         // 32 KB (D=128)
+  static constexpr int Q_BYTES = BQ * D * 2;
   static constexpr int K_BYTES = BKV * D * 2;
   static constexpr int V_BYTES = BKV * D * 2;
-  static constexpr int P_BYTES = BQ * BKV * 2;       // 32 KB
+  static constexpr int P_BYTES = BQ * BKV * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;      // 2 stages
   static constexpr int OFF_V = OFF_K + 2 * K_BYTES;  // 2 stages
-  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;  // 2 buffers
+  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;  // P[0] even blocks, P[1] odd blocks
   static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
-  static constexpr int THREADS = 192;
-  static constexpr uint32_t TMEM_COLS = 512;          // S0 [0,128) S1 [128,256) O [256, 256+D)
+  static_assert(SMEM <= 232448, "forward tile set exceeds the 227 KB shared-memory limit");
+  static constexpr int THREADS = 320;
+  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D)
+  static constexpr uint32_t T_S = 0, T_O = 256, TMEM_COLS = 512;
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
   using C = FwdCfg<D>;
@@ -105,11 +107,11 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* k_empty = bar + 3;  // [2]
   uint64_t* v_full = bar + 5;   // [2]
   uint64_t* v_empty = bar + 7;  // [2]
-  uint64_t* s_full = bar + 9;   // [2]
-  uint64_t* p_full = bar + 11;  // [2]
-  uint64_t* o_upd = bar + 13;   // PV done (one phase per KV block)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 15);
+  uint64_t* s_full = bar + 9;   // [2] S of block j into S[j&1]
+  uint64_t* p_full = bar + 11;  // [2] P of block j into P[j&1] (count 128)
+  uint64_t* o_upd = bar + 13;   // [2] PV of block j into O[j&1] done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * C::BQ;
@@ -126,8 +128,8 @@ __global__ void __launch_bounds__(192, 1)
       tc::mbar_init(&v_empty[i], 1);
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 128);
+      tc::mbar_init(&o_upd[i], 1);
     }
-    tc::mbar_init(o_upd, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -139,7 +141,6 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t t_o = tbase + 256;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (k >> 2) * (128 * 128) + (k & 3) * 32;
-          tc::mma_f16_ss(tbase + s * 128, tc::sdesc_sw128(q_addr + off, 16, 1024),
+          tc::mma_f16_ss(tbase + C::T_S + s * 128, tc::sdesc_sw128(q_addr + off, 16, 1024),
                          tc::sdesc_sw128(k_addr + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
         }
         tc::mma_commit(&s_full[s]);
@@ -209,38 +210,44 @@ __global__ void __launch_bounds__(192, 1)
         for (int k = 0; k < C::BKV / 16; ++k) {
           const uint64_t ad = tc::sdesc_sw128(p_addr + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024);
           const uint64_t bd = tc::sdesc_sw128(v_addr + k * 2048, C::BKV * 128, 1024);
-          tc::mma_f16_ss(t_o, ad, bd, IDESC_O, (j > 0 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ss(tbase + C::T_O + s * 128, ad, bd, IDESC_O, (j >= 2 || k > 0) ? 1u : 0u);
         }
-        tc::mma_commit(o_upd);
+        tc::mma_commit(&o_upd[s]);
         tc::mma_commit(&v_empty[s]);
         if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
       }
       if (!ok) *abort_flag = 1;
     }
   } else {
-    // ---------------- softmax + epilogue: warps 2..5, thread = query row ----------------
+    // ---------------- softmax warpgroups: g = 0 takes even KV blocks, g = 1 odd ones ----------------
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // row inside the tile == TMEM lane
+    const int r = quarter * 32 + lane;  // query row inside the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_s = tbase + C::T_S + g * 128, t_o = tbase + C::T_O + g * 128;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      const int s = j & 1;
-      if (!tc::mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1), p.err) || *abort_flag) {
+    int kb = 0;  // blocks processed by this warpgroup
+    for (int j = g; j < nblk; j += 2, ++kb) {
+      if (!tc::mbar_wait(&s_full[g], (uint32_t)(kb & 1), p.err) || *abort_flag) {
         ok = false;
         break;
       }
       tc::tc_fence_after();
-      uint32_t sr[128];
-      __syncwarp();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::tmem_ld32(tbase + s * 128 + c * 32 + lane_off, sr + c * 32);
-      tc::tmem_wait_ld();
-      const int valid = (int)(p.Sk - (int64_t)j * C::BKV < C::BKV ? p.Sk - (int64_t)j * C::BKV : C::BKV);
+      const int64_t rem = p.Sk - (int64_t)j * C::BKV;
+      const int valid = rem < C::BKV ? (int)rem : C::BKV;
+      // pass 1: row max, 32 columns at a time (S stays in TMEM; it is re-read in pass 2)
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c)
-        if (c < valid) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        __syncwarp();
+        tc::tmem_ld32(t_s + c * 32 + lane_off, sr);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(sr[e]));
+      }
       const float m_blk = mx * p.scale_log2;
       // lazy rescale: keep the old max unless the new one is more than 2^8 larger
       const bool need = (m == -INFINITY) || (m_blk > m + 8.f);
@@ -250,9 +257,9 @@ __global__ void __launch_bounds__(192, 1)
         alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
         m = m_new;
       }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O holds the sum up to PV_{j-1}; wait for it, then scale this warp's rows in TMEM
-        if (!tc::mbar_wait(o_upd, (uint32_t)((j - 1) & 1), p.err)) {
+      if (kb > 0 && __any_sync(0xffffffffu, need)) {
+        // O[g] holds this group's sum up to its previous block: wait for that PV, then scale in TMEM
+        if (!tc::mbar_wait(&o_upd[g], (uint32_t)((kb - 1) & 1), p.err)) {
           ok = false;
           break;
         }
@@ -270,52 +277,79 @@ __global__ void __launch_bounds__(192, 1)
         tc::tmem_wait_st();
       }
       l *= alpha;
-      // P = exp2(s * scale_log2 - m), written as bf16 into the swizzled A tile of the PV MMA
-      uint8_t* ptile = smem + C::OFF_P + s * C::P_BYTES;
+      uint8_t* ptile = smem + C::OFF_P + g * C::P_BYTES;
       float rowsum = 0.f;
 #pragma unroll
-      for (int g = 0; g < 16; ++g) {  // 16 granules of 8 keys
-        uint32_t w[4];
+      for (int c = 0; c < 4; ++c) {  // pass 2: P = exp2(s * scale_log2 - m) as bf16 into the PV A tile
+        uint32_t sr[32];
+        __syncwarp();
+        tc::tmem_ld32(t_s + c * 32 + lane_off, sr);
+        tc::tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c0 = g * 8 + 2 * e;
-          float p0 = c0 < valid ? ex2(__uint_as_float(sr[c0]) * p.scale_log2 - m) : 0.f;
-          float p1 = c0 + 1 < valid ? ex2(__uint_as_float(sr[c0 + 1]) * p.scale_log2 - m) : 0.f;
-          rowsum += p0 + p1;
-          w[e] = pack2(p0, p1, BF16);
+        for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 keys
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i0 = q4 * 8 + 2 * e, c0 = c * 32 + i0;
+            float p0 = c0 < valid ? ex2(__uint_as_float(sr[i0]) * p.scale_log2 - m) : 0.f;
+            float p1 = c0 + 1 < valid ? ex2(__uint_as_float(sr[i0 + 1]) * p.scale_log2 - m) : 0.f;
+            rowsum += p0 + p1;
+            w[e] = pack2(p0, p1, BF16);
+          }
+          const int gr = c * 4 + q4;
+          uint8_t* row = ptile + (gr >> 3) * (128 * 128) + r * 128;
+          *reinterpret_cast<uint4*>(row + (((gr & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        uint8_t* row = ptile + (g >> 3) * (128 * 128) + r * 128;
-        *reinterpret_cast<uint4*>(row + (((g & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       l += rowsum;
       tc::fence_async_shared();
       tc::tc_fence_before();
-      tc::mbar_arrive(&p_full[s]);
+      tc::mbar_arrive(&p_full[g]);
     }
-    // ---------------- epilogue: O / l -> global, lse ----------------
-    if (ok && tc::mbar_wait(o_upd, (uint32_t)((nblk - 1) & 1), p.err)) {
+    // ---------------- epilogue: combine the two groups, O / l -> global, lse ----------------
+    const int nb0 = (nblk + 1) / 2, nb1 = nblk / 2;
+    if (ok && kb > 0 && !tc::mbar_wait(&o_upd[g], (uint32_t)((kb - 1) & 1), p.err)) ok = false;
+    // (m, l) exchange through the start of each group's own P buffer: its last PV has completed
+    float2* x0p = reinterpret_cast<float2*>(smem + C::OFF_P);
+    float2* x1p = reinterpret_cast<float2*>(smem + C::OFF_P + C::P_BYTES);
+    (g ? x1p : x0p)[r] = make_float2(m, l);
+    tc::named_bar_sync(1, 256);
+    if (ok && !*abort_flag) {
       tc::tc_fence_after();
+      const float2 x0 = x0p[r], x1 = x1p[r];
+      const float M = fmaxf(x0.x, x1.x);
+      const float a0 = nb0 > 0 ? ex2(x0.x - M) : 0.f;
+      const float a1 = nb1 > 0 ? ex2(x1.x - M) : 0.f;
+      const float L = x0.y * a0 + x1.y * a1;
+      const float s0 = a0 / L, s1 = a1 / L;
       const int64_t qrow = q0 + r;
-      const float inv = 1.f / l;
       using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       T* orow = (T*)p.o + (int64_t)b * p.o_s[0] + (int64_t)h * p.o_s[1] + qrow * p.o_s[2];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t ov[32];
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int c = g * (D / 64) + cc;  // this group's 32-column chunks
+        uint32_t o0[32], o1[32];
         __syncwarp();
-        tc::tmem_ld32(t_o + c * 32 + lane_off, ov);
+        tc::tmem_ld32(tbase + C::T_O + c * 32 + lane_off, o0);
+        if (nb1 > 0) tc::tmem_ld32(tbase + C::T_O + 128 + c * 32 + lane_off, o1);
         tc::tmem_wait_ld();
         if (qrow < p.Sq) {
           uint32_t w[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            w[e] = pack2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv, BF16);
+          for (int e = 0; e < 16; ++e) {
+            float v0 = __uint_as_float(o0[2 * e]) * s0, v1 = __uint_as_float(o0[2 * e + 1]) * s0;
+            if (nb1 > 0) {
+              v0 += __uint_as_float(o1[2 * e]) * s1;
+              v1 += __uint_as_float(o1[2 * e + 1]) * s1;
+            }
+            w[e] = pack2(v0, v1, BF16);
+          }
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         }
       }
-      if (qrow < p.Sq) p.lse[(int64_t)bh * p.Sq + qrow] = (m + __log2f(l)) * 0.6931471805599453f;
+      if (g == 0 && qrow < p.Sq) p.lse[(int64_t)bh * p.Sq + qrow] = (M + __log2f(L)) * 0.6931471805599453f;
     } else {
       *abort_flag = 1;
     }
@@ -405,46 +439,51 @@ int attn_simt_bwd_dispatch(const b2_attn_args* a, cudaStream_t st);  // attn_sim
 namespace {
 
 // ==================================================================================================
-// backward (D = 128): one CTA per (128-key tile, batch*head), walking 64-query tiles
+// backward (D = 128): one CTA per (128-key tile, batch*head), walking 64-query tiles; two compute
+// warpgroups split each tile's 64 query columns (elementwise work needs no cross-group reduction)
 // ==================================================================================================
 struct BwdCfg {
   static constexpr int D = 128, BKV = 128, BQ = 64;
   static constexpr int KV_BYTES = BKV * D * 2;        // K or V tile, 32 KB
   static constexpr int QT_BYTES = BQ * D * 2;         // Q or dO tile, 16 KB
   static constexpr int PT_BYTES = BKV * BQ * 2;       // P^T or dS^T tile, 16 KB
+  static constexpr int LD_BYTES = BQ * 8;             // (lse*log2e, delta) per query
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + KV_BYTES;
   static constexpr int OFF_Q = OFF_V + KV_BYTES;      // 2 stages
   static constexpr int OFF_DO = OFF_Q + 2 * QT_BYTES; // 2 stages
   static constexpr int OFF_P = OFF_DO + 2 * QT_BYTES; // 2 buffers
   static constexpr int OFF_DS = OFF_P + 2 * PT_BYTES; // 2 buffers
-  static constexpr int OFF_BAR = OFF_DS + 2 * PT_BYTES;
+  static constexpr int OFF_LD = OFF_DS + 2 * PT_BYTES; // 2 stages
+  static constexpr int OFF_BAR = OFF_LD + 2 * LD_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
-  static constexpr int THREADS = 192;
+  static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KB shared-memory limit");
+  static constexpr int THREADS = 320;
   // TMEM columns: S^T [0,64) dP^T [64,128) dQ^T [128,192) dV [256,384) dK [384,512)
   static constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_DV = 256, T_DK = 384, TMEM_COLS = 512;
 };
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                       AttnTcParams p, int bf16_flag) {
+                       AttnTcParams p, const float2* __restrict__ lsed, int64_t sq_pad) {
   using C = BwdCfg;
+  constexpr bool BF16 = true;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* kv_full = bar + 0;
-  uint64_t* q_full = bar + 1;     // [2] Q_i + dO_i landed
+  uint64_t* q_full = bar + 1;     // [2] Q_i, dO_i, (lse, delta)_i landed
   uint64_t* q_empty = bar + 3;    // [2] all MMAs reading Q_i / dO_i done
   uint64_t* sdp_full = bar + 5;   // S^T_i and dP^T_i in TMEM
-  uint64_t* pds_full = bar + 6;   // [2] P^T_i / dS^T_i written (count 128)
+  uint64_t* pds_full = bar + 6;   // [2] P^T_i / dS^T_i written (count 256)
   uint64_t* pds_empty = bar + 8;  // [2] MMAs reading P^T_i / dS^T_i done
   uint64_t* dq_full = bar + 10;   // dQ^T_i in TMEM
-  uint64_t* dq_empty = bar + 11;  // dQ^T_i drained (count 128)
+  uint64_t* dq_empty = bar + 11;  // dQ^T_i drained (count 256)
   uint64_t* dkv_full = bar + 12;  // final dK, dV in TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 14);
-  const bool BF16 = bf16_flag != 0;
+  uint64_t* sdp_empty = bar + 13; // S^T_i / dP^T_i loaded into registers (count 256)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 15);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = blockIdx.x * C::BKV;
@@ -457,13 +496,14 @@ __global__ void __launch_bounds__(192, 1)
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&q_full[i], 1);
       tc::mbar_init(&q_empty[i], 1);
-      tc::mbar_init(&pds_full[i], 128);
+      tc::mbar_init(&pds_full[i], 256);
       tc::mbar_init(&pds_empty[i], 1);
     }
     tc::mbar_init(sdp_full, 1);
     tc::mbar_init(dq_full, 1);
-    tc::mbar_init(dq_empty, 128);
+    tc::mbar_init(dq_empty, 256);
     tc::mbar_init(dkv_full, 1);
+    tc::mbar_init(sdp_empty, 256);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -478,7 +518,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: K, V once; Q_i, dO_i into a 2-stage ring ----------------
+      // ---------------- producer: K, V once; Q_i, dO_i, (lse, delta)_i into a 2-stage ring ----------------
       tc::mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
       for (int c = 0; c < 2; ++c) {
         tc::tma_load_4d(smem + C::OFF_K + c * (C::BKV * 128), &tmK, kv_full, c * 64, k0, h, b);
@@ -492,11 +532,13 @@ __global__ void __launch_bounds__(192, 1)
           ok = false;
           break;
         }
-        tc::mbar_arrive_expect_tx(&q_full[s], 2 * C::QT_BYTES);
+        tc::mbar_arrive_expect_tx(&q_full[s], 2 * C::QT_BYTES + C::LD_BYTES);
         for (int c = 0; c < 2; ++c) {
           tc::tma_load_4d(smem + C::OFF_Q + s * C::QT_BYTES + c * (C::BQ * 128), &tmQ, &q_full[s], c * 64, i * C::BQ, h, b);
           tc::tma_load_4d(smem + C::OFF_DO + s * C::QT_BYTES + c * (C::BQ * 128), &tmDO, &q_full[s], c * 64, i * C::BQ, h, b);
         }
+        tc::bulk_load(smem + C::OFF_LD + s * C::LD_BYTES, lsed + (int64_t)bh * sq_pad + (int64_t)i * C::BQ, C::LD_BYTES,
+                      &q_full[s]);
         issued[s]++;
       }
       if (!ok) {
@@ -509,9 +551,9 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t IDESC_SDP = tc::idesc_f16(128, C::BQ, BF16, false, false);  // K Q^T, V dO^T: both K-major
-      const uint32_t IDESC_KV = tc::idesc_f16(128, C::D, BF16, false, true);     // P^T dO, dS^T Q: B MN-major
-      const uint32_t IDESC_DQ = tc::idesc_f16(128, C::BQ, BF16, true, true);     // K^T dS^T: A and B MN-major
+      constexpr uint32_t IDESC_SDP = tc::idesc_f16(128, C::BQ, BF16, false, false);  // K Q^T, V dO^T: K-major
+      constexpr uint32_t IDESC_KV = tc::idesc_f16(128, C::D, BF16, false, true);     // P^T dO, dS^T Q: B MN-major
+      constexpr uint32_t IDESC_DQ = tc::idesc_f16(128, C::BQ, BF16, true, true);     // K^T dS^T: A, B MN-major
       const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K), v_addr = tc::smem_u32(smem + C::OFF_V);
       bool ok = tc::mbar_wait(kv_full, 0, p.err);
       auto issue_sdp = [&](int i) -> bool {
@@ -541,34 +583,33 @@ __global__ void __launch_bounds__(192, 1)
       for (int i = 0; i < ntile && ok; ++i) {
         const int s = i & 1;
         const uint32_t ph = (uint32_t)((i >> 1) & 1);
+        // as soon as S^T_i / dP^T_i are in registers, the next tile's scores can go into TMEM
+        if (!tc::mbar_wait(sdp_empty, (uint32_t)(i & 1), p.err)) { ok = false; break; }
+        tc::tc_fence_after();
+        if (i + 1 < ntile && !issue_sdp(i + 1)) { ok = false; break; }
         if (!tc::mbar_wait(&pds_full[s], ph, p.err)) { ok = false; break; }
         tc::tc_fence_after();
-        // the softmax threads have read S^T_i / dP^T_i: the next tile's scores can go into TMEM now
-        if (i + 1 < ntile && !issue_sdp(i + 1)) { ok = false; break; }
         const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES);
         const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES);
         const uint32_t pt_addr = tc::smem_u32(smem + C::OFF_P + s * C::PT_BYTES);
         const uint32_t ds_addr = tc::smem_u32(smem + C::OFF_DS + s * C::PT_BYTES);
         // dV += P^T dO ; dK += dS^T Q   (M = 128 keys, N = D, K = 64 queries)
 #pragma unroll
-        for (int k = 0; k < C::BQ / 16; ++k) {
+        for (int k = 0; k < C::BQ / 16; ++k)
           tc::mma_f16_ss(tbase + C::T_DV, tc::sdesc_sw128(pt_addr + k * 32, 16, 1024),
                          tc::sdesc_sw128(do_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
-        }
 #pragma unroll
-        for (int k = 0; k < C::BQ / 16; ++k) {
+        for (int k = 0; k < C::BQ / 16; ++k)
           tc::mma_f16_ss(tbase + C::T_DK, tc::sdesc_sw128(ds_addr + k * 32, 16, 1024),
                          tc::sdesc_sw128(q_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
-        }
         tc::mma_commit(&q_empty[s]);
         // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
         if (i > 0 && !tc::mbar_wait(dq_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
         tc::tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < C::BKV / 16; ++k) {
+        for (int k = 0; k < C::BKV / 16; ++k)
           tc::mma_f16_ss(tbase + C::T_DQ, tc::sdesc_sw128(k_addr + k * 2048, C::BKV * 128, 1024),
                          tc::sdesc_sw128(ds_addr + k * 2048, 8192, 1024), IDESC_DQ, k > 0 ? 1u : 0u);
-        }
         tc::mma_commit(dq_full);
         tc::mma_commit(&pds_empty[s]);
       }
@@ -576,69 +617,69 @@ __global__ void __launch_bounds__(192, 1)
       else *abort_flag = 1;
     }
   } else {
-    // ---------------- warps 2..5: P^T / dS^T (thread = key row), dQ drain, dK/dV epilogue -----------
+    // ---------------- warps 2..9: P^T / dS^T, dQ drain, dK/dV epilogue ----------------
+    // thread = key row r (TMEM lane; also d for dQ^T); group g owns query columns [32g, 32g+32)
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // key row within the tile == TMEM lane (also d for dQ^T)
+    const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const float LOG2E = 1.4426950408889634f;
     bool ok = true;
     auto drain_dq = [&](int i) -> bool {
       if (!tc::mbar_wait(dq_full, (uint32_t)(i & 1), p.err)) return false;
       tc::tc_fence_after();
-      uint32_t v[64];
+      uint32_t v[32];
       __syncwarp();
-      tc::tmem_ld32(tbase + C::T_DQ + lane_off, v);
-      tc::tmem_ld32(tbase + C::T_DQ + 32 + lane_off, v + 32);
+      tc::tmem_ld32(tbase + C::T_DQ + g * 32 + lane_off, v);
       tc::tmem_wait_ld();
       tc::tc_fence_before();
       tc::mbar_arrive(dq_empty);
-      // dq_acc layout [bh][d][Sq_pad]: thread d adds 64 consecutive queries
-      const int64_t sq_pad = (p.Sq + 63) / 64 * 64;
-      float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * C::D + r) * sq_pad + (int64_t)i * C::BQ);
+      // dq_acc layout [bh][d][sq_pad]: thread d adds its 32 consecutive queries
+      float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * C::D + r) * sq_pad + (int64_t)i * C::BQ + g * 32);
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
+      for (int e = 0; e < 8; ++e)
         atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]) * p.scale, __uint_as_float(v[4 * e + 1]) * p.scale,
                                        __uint_as_float(v[4 * e + 2]) * p.scale, __uint_as_float(v[4 * e + 3]) * p.scale));
       return true;
     };
     for (int i = 0; i < ntile; ++i) {
       const int s = i & 1;
-      if (!tc::mbar_wait(sdp_full, (uint32_t)(i & 1), p.err) || *abort_flag) { ok = false; break; }
+      if (!tc::mbar_wait(sdp_full, (uint32_t)(i & 1), p.err) || !tc::mbar_wait(&q_full[s], (uint32_t)((i >> 1) & 1), p.err) ||
+          *abort_flag) {
+        ok = false;
+        break;
+      }
       tc::tc_fence_after();
-      uint32_t sv[64], dp[64];
+      uint32_t sv[32], dp[32];
       __syncwarp();
-      tc::tmem_ld32(tbase + C::T_S + lane_off, sv);
-      tc::tmem_ld32(tbase + C::T_S + 32 + lane_off, sv + 32);
-      tc::tmem_ld32(tbase + C::T_DP + lane_off, dp);
-      tc::tmem_ld32(tbase + C::T_DP + 32 + lane_off, dp + 32);
+      tc::tmem_ld32(tbase + C::T_S + g * 32 + lane_off, sv);
+      tc::tmem_ld32(tbase + C::T_DP + g * 32 + lane_off, dp);
       tc::tmem_wait_ld();
+      tc::tc_fence_before();
+      tc::mbar_arrive(sdp_empty);
       // P^T / dS^T buffer s was last read by the MMAs of tile i-2
       if (i >= 2 && !tc::mbar_wait(&pds_empty[s], (uint32_t)(((i - 2) >> 1) & 1), p.err)) { ok = false; break; }
-      const int64_t qbase = (int64_t)i * C::BQ;
-      const float* lse_row = p.lse + (int64_t)bh * p.Sq;
-      const float* dl_row = p.delta + (int64_t)bh * p.Sq;
+      const float2* ld = reinterpret_cast<const float2*>(smem + C::OFF_LD + s * C::LD_BYTES) + g * 32;
       uint8_t* pt = smem + C::OFF_P + s * C::PT_BYTES + r * 128;
       uint8_t* dst = smem + C::OFF_DS + s * C::PT_BYTES + r * 128;
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
+      for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 queries
         uint32_t wp[4], wd[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float pv[2], dv[2];
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            const int c = g * 8 + 2 * e + t;
-            const int64_t qi = qbase + c;
-            float L = qi < p.Sq ? __ldg(lse_row + qi) * LOG2E : INFINITY;
-            float dl = qi < p.Sq ? __ldg(dl_row + qi) : 0.f;
-            float pp = ex2(__uint_as_float(sv[c]) * p.scale_log2 - L);
+            const int c = q4 * 8 + 2 * e + t;
+            const float2 L = ld[c];  // (lse * log2e, delta); padding rows hold (+inf, 0)
+            const float pp = ex2(__uint_as_float(sv[c]) * p.scale_log2 - L.x);
             pv[t] = pp;
-            dv[t] = pp * (__uint_as_float(dp[c]) - dl);
+            dv[t] = pp * (__uint_as_float(dp[c]) - L.y);
           }
           wp[e] = pack2(pv[0], pv[1], BF16);
           wd[e] = pack2(dv[0], dv[1], BF16);
         }
-        const int off = ((g ^ (r & 7)) << 4);
+        const int gr = g * 4 + q4;
+        const int off = ((gr ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(pt + off) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
         *reinterpret_cast<uint4*>(dst + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
       }
@@ -648,18 +689,18 @@ __global__ void __launch_bounds__(192, 1)
       if (i > 0 && !drain_dq(i - 1)) { ok = false; break; }
     }
     if (ok && ntile > 0) ok = drain_dq(ntile - 1);
-    // ---------------- dK, dV epilogue ----------------
+    // ---------------- dK, dV epilogue: group g writes d columns [64g, 64g+64) ----------------
     if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
       tc::tc_fence_after();
       const int64_t krow = k0 + r;
-      using Tb = __nv_bfloat16;
       for (int which = 0; which < 2; ++which) {  // 0: dV, 1: dK (times scale)
         void* base = which ? p.dk : p.dv;
         const int64_t* st = which ? p.dk_s : p.dv_s;
         const float mul = which ? p.scale : 1.f;
         const uint32_t tcol = which ? C::T_DK : C::T_DV;
 #pragma unroll
-        for (int c = 0; c < C::D / 32; ++c) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = g * 2 + cc;
           uint32_t v[32];
           __syncwarp();
           tc::tmem_ld32(tbase + tcol + c * 32 + lane_off, v);
@@ -669,8 +710,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e)
               w[e] = pack2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul, BF16);
-            uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<Tb*>(base) + (int64_t)b * st[0] + (int64_t)h * st[1] +
-                                                 krow * st[2] + c * 32);
+            uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + (int64_t)b * st[0] +
+                                                 (int64_t)h * st[1] + krow * st[2] + c * 32);
 #pragma unroll
             for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
           }
@@ -690,21 +731,76 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// dq[b,h,q,d] = dq_acc[bh][d][q] (fp32 -> T), 32x32 tiles transposed through shared memory.
-template <typename T>
-__global__ void dq_convert(const float* __restrict__ acc, T* __restrict__ dq, int64_t H, int64_t Sq, int64_t sq_pad,
-                           int64_t D, int64_t s0, int64_t s1, int64_t s2) {
-  __shared__ float tile[32][33];
-  const int64_t bh = blockIdx.z, b = bh / H, h = bh % H;
-  const int64_t q0 = (int64_t)blockIdx.x * 32, d0 = (int64_t)blockIdx.y * 32;
-  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
-    int64_t d = d0 + y, q = q0 + threadIdx.x;
-    tile[y][threadIdx.x] = (d < D && q < Sq) ? acc[(bh * D + d) * sq_pad + q] : 0.f;
+// Pre-pass, one block per (64-query tile, batch*head): lsed[bh][q] = (lse*log2e, rowsum(O*dO)) with
+// (+inf, 0) for padding rows, and zero the tile's slice of the fp32 dQ accumulator [bh][d][sq_pad].
+__global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
+                                                     const float* __restrict__ lse, float2* __restrict__ lsed,
+                                                     float* __restrict__ dq_acc, int64_t H, int64_t Sq, int64_t sq_pad,
+                                                     int64_t o0, int64_t o1, int64_t o2, int64_t g0, int64_t g1, int64_t g2) {
+  const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int64_t q0 = (int64_t)blockIdx.x * 64;
+  // thread = (row, quarter of the 128-wide row): 4 x 16-byte loads of O and of dO, all in flight at once
+  const int row = threadIdx.x >> 2, qtr = threadIdx.x & 3;
+  const int64_t q = q0 + row;
+  float s = 0.f;
+  if (q < Sq) {
+    const uint4* op = reinterpret_cast<const uint4*>(o + b * o0 + h * o1 + q * o2) + qtr * 4;
+    const uint4* gp = reinterpret_cast<const uint4*>(d_o + b * g0 + h * g1 + q * g2) + qtr * 4;
+    uint4 a[4], c[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[e] = __ldg(op + e), c[e] = __ldg(gp + e);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a[e]);
+      const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&c[e]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 x = __bfloat1622float2(a2[k]), y = __bfloat1622float2(c2[k]);
+        s += x.x * y.x + x.y * y.y;
+      }
+    }
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  if (qtr == 0)
+    lsed[bh * sq_pad + q] = q < Sq ? make_float2(lse[bh * Sq + q] * 1.4426950408889634f, s) : make_float2(INFINITY, 0.f);
+  float4* acc = reinterpret_cast<float4*>(dq_acc + bh * 128 * sq_pad + q0);
+  const int64_t row4 = sq_pad / 4;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int e = threadIdx.x + it * 256;  // 128 d-rows x 16 float4
+    acc[(e >> 4) * row4 + (e & 15)] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// dq[b,h,q,:] = bf16(dq_acc[bh][:][q]), one block per (64-query tile, batch*head), transposed through
+// shared memory so both the fp32 reads and the bf16 writes are 16-byte and coalesced.
+__global__ void __launch_bounds__(256) attn_dq_convert(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dq,
+                                                       int64_t H, int64_t Sq, int64_t sq_pad, int64_t s0, int64_t s1,
+                                                       int64_t s2) {
+  __shared__ float t[128][65];
+  const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int64_t q0 = (int64_t)blockIdx.x * 64;
+  const float4* src = reinterpret_cast<const float4*>(dq_acc + bh * 128 * sq_pad + q0);
+  const int64_t row4 = sq_pad / 4;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int e = threadIdx.x + it * 256;
+    const int d = e >> 4, j = (e & 15) * 4;
+    float4 v = src[d * row4 + (e & 15)];
+    t[d][j] = v.x, t[d][j + 1] = v.y, t[d][j + 2] = v.z, t[d][j + 3] = v.w;
   }
   __syncthreads();
-  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
-    int64_t q = q0 + y, d = d0 + threadIdx.x;
-    if (q < Sq && d < D) dq[b * s0 + h * s1 + q * s2 + d] = from_f32<T>(tile[threadIdx.x][y]);
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = threadIdx.x + it * 256;  // 64 rows x 16 chunks of 8 d
+    const int j = e >> 4, d0 = (e & 15) * 8;
+    const int64_t q = q0 + j;
+    if (q >= Sq) continue;
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = pack2(t[d0 + 2 * k][j], t[d0 + 2 * k + 1][j], true);
+    *reinterpret_cast<uint4*>(dq + b * s0 + h * s1 + q * s2 + d0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -713,22 +809,25 @@ __global__ void dq_convert(const float* __restrict__ acc, T* __restrict__ dq, in
 bool attn_tc_bwd_eligible(const b2_attn_args* a) {
   if (!attn_tc_eligible(a) || a->D != 128 || a->dtype != B2_BF16) return false;
   if (!strides_ok(a->do_s, a->B, a->H, a->Sq) || ((uintptr_t)a->d_o & 15)) return false;
+  if ((a->do_s[2] % 8) || (a->do_s[1] % 8) || (a->do_s[0] % 8)) return false;
   auto al = [](const void* p) { return p == nullptr || ((uintptr_t)p & 15) == 0; };
-  if (!al(a->dk) || !al(a->dv)) return false;
+  if (!al(a->dk) || !al(a->dv) || !al(a->dq)) return false;
   for (int i = 0; i < 3; ++i)
-    if ((a->dk && a->dk_s[i] % 8) || (a->dv && a->dv_s[i] % 8)) return false;
+    if ((a->dk && a->dk_s[i] % 8) || (a->dv && a->dv_s[i] % 8) || (a->dq && a->dq_s[i] % 8)) return false;
   return true;
 }
 
+// workspace = fp32 dQ accumulator [B*H][D][sq_pad] followed by (lse*log2e, delta) [B*H][sq_pad]
 uint64_t attn_bwd_ws_bytes(const b2_attn_args* a) {
   if (!attn_tc_bwd_eligible(a)) return 0;
   const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
-  return (uint64_t)(a->B * a->H) * (uint64_t)a->D * (uint64_t)sq_pad * 4;
+  return (uint64_t)(a->B * a->H) * (uint64_t)sq_pad * (uint64_t)(a->D * 4 + 8);
 }
 
 int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   if (!attn_tc_bwd_eligible(a)) return attn_simt_bwd_dispatch(a, st);
-  if (!a->workspace) return fail(B2_ERR_ARG, "attn_bwd: workspace of b2_attn_bwd_workspace_bytes() required");
+  if (!a->workspace || ((uintptr_t)a->workspace & 15))
+    return fail(B2_ERR_ARG, "attn_bwd: a 16-byte aligned workspace of b2_attn_bwd_workspace_bytes() is required");
   using C = BwdCfg;
   static bool attr = false;
   if (!attr) {
@@ -737,9 +836,17 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
       return rc;
     attr = true;
   }
-  if (int rc = attn_delta_launch(a, st)) return rc;
-  const uint64_t ws = attn_bwd_ws_bytes(a);
-  if (int rc = check_cuda(cudaMemsetAsync(a->workspace, 0, ws, st), "attn_bwd: clear dQ accumulator")) return rc;
+  const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
+  float* dq_acc = (float*)a->workspace;
+  float2* lsed = reinterpret_cast<float2*>(dq_acc + a->B * a->H * a->D * sq_pad);
+  {
+    dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
+    LaunchScope ls("attn_bwd_prep", st);
+    attn_bwd_prep<<<grid, 256, 0, st>>>((const __nv_bfloat16*)a->o, (const __nv_bfloat16*)a->d_o, a->lse, lsed, dq_acc,
+                                        a->H, a->Sq, sq_pad, a->o_s[0], a->o_s[1], a->o_s[2], a->do_s[0], a->do_s[1],
+                                        a->do_s[2]);
+    if (int rc = after_launch("attn_bwd_prep")) return rc;
+  }
   CUtensorMap tq, tk, tv, tdo;
   if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, 128, true, 64) ||
       !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, 128, true, 128) ||
@@ -751,23 +858,21 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   p.scale = a->scale;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.lse = a->lse;
-  p.delta = a->delta;
-  p.dq_acc = (float*)a->workspace;
+  p.dq_acc = dq_acc;
   p.dk = a->dk, p.dv = a->dv;
   for (int i = 0; i < 3; ++i) p.dk_s[i] = a->dk_s[i], p.dv_s[i] = a->dv_s[i];
   p.err = device_error_ptr();
   {
     dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)(a->B * a->H));
     LaunchScope ls("attn_bwd_tc", st);
-    attn_bwd_tc_kernel<<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, tdo, p, 1);
+    attn_bwd_tc_kernel<<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, tdo, p, lsed, sq_pad);
     if (int rc = after_launch("attn_bwd_tc")) return rc;
   }
   if (a->dq) {
-    const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
-    dim3 grid((unsigned)((a->Sq + 31) / 32), (unsigned)((a->D + 31) / 32), (unsigned)(a->B * a->H));
+    dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
     LaunchScope ls("attn_dq_convert", st);
-    dq_convert<__nv_bfloat16><<<grid, dim3(32, 8), 0, st>>>((const float*)a->workspace, (__nv_bfloat16*)a->dq, a->H,
-                                                            a->Sq, sq_pad, a->D, a->dq_s[0], a->dq_s[1], a->dq_s[2]);
+    attn_dq_convert<<<grid, 256, 0, st>>>(dq_acc, (__nv_bfloat16*)a->dq, a->H, a->Sq, sq_pad, a->dq_s[0], a->dq_s[1],
+                                          a->dq_s[2]);
     if (int rc = after_launch("attn_dq_convert")) return rc;
   }
   return 0;

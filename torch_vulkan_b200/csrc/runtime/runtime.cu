@@ -156,6 +156,17 @@ int* device_error_ptr() {
 
 void stat_add(int id, uint64_t v) { g_stats[id].fetch_add(v, std::memory_order_relaxed); }
 
+namespace {
+// Spins one thread for `ns` nanoseconds of %globaltimer (bounded by construction).
+__global__ void gpu_sleep_kernel(uint64_t ns) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  do {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  } while (t - t0 < ns);
+}
+}  // namespace
+
 }  // namespace b2
 
 using namespace b2;
@@ -251,6 +262,13 @@ size_t b2rt_profile_dump(char* buf, size_t cap) {
     buf[n] = 0;
   }
   return s.size();
+}
+
+int b2rt_gpu_sleep(uint64_t ns, b2_stream_t stream) {
+  if (int rc = ensure_init()) return rc;
+  if (ns > 1000000000ull) return fail(B2_ERR_ARG, "gpu_sleep: at most 1 s");
+  gpu_sleep_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(ns);
+  return after_launch("b2rt_gpu_sleep");
 }
 
 int b2rt_synchronize(void) {
