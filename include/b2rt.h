@@ -283,6 +283,17 @@ typedef struct b2_layernorm_args {
 int b2_layernorm_fwd(const b2_layernorm_args* args, b2_stream_t stream);
 int b2_layernorm_bwd(const b2_layernorm_args* args, b2_stream_t stream);
 uint64_t b2_layernorm_bwd_workspace_bytes(const b2_layernorm_args* args);
+/* LayerNorm backward that allocates nothing (no counterpart in the reference). For callers that
+ * cannot allocate device memory mid-step: a host framework that owns all VRAM through its own
+ * allocator or a fixed budget, or an FFI caller that only holds the tensors. Same arguments and
+ * results as b2_layernorm_bwd except that args->workspace is ignored: the dw/db partial sums go to a
+ * 2 MiB scratch array compiled into the library (kept by every GPU that loads it until exit), so
+ * D <= 262144 when dw or db is requested; larger D is rejected with B2_ERR_ARG. The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress), so make it before any CUDA
+ * graph capture. Every call reuses the same array: calls that can overlap on the GPU (different
+ * streams, no ordering between them) race; calls ordered on one stream are safe. Nothing in the
+ * array needs to start at zero (every partial is written before it is read). */
+int b2_layernorm_bwd_noalloc(const b2_layernorm_args* args, b2_stream_t stream);
 
 /* Optimizer ternaries (csrc/ops_ew.cpp:405-455, expressions tools/gen_shaders.py:83-92):
  *   op 0 addcmul: out = x + value * t1 * t2

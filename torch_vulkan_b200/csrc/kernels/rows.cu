@@ -8,6 +8,9 @@
 // ideal HBM traffic of one read and one write per element. LayerNorm weight/bias gradients are a
 // two-stage column reduction (per-row-group partials, then a column sum) instead of the
 // reference's one-thread-per-column loop over all rows (ln.comp.in:27-38).
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 
 namespace b2 {
@@ -698,6 +701,68 @@ int ln_entry(const b2_layernorm_args* a, b2_stream_t stream, bool fwd) {
   }
 }
 
+// ---- allocation-free LayerNorm backward ---------------------------------------------------------
+// Some callers cannot allocate device memory in the middle of a step: a host framework that owns
+// every byte of VRAM through its own allocator or a fixed budget, or an FFI caller that only holds the
+// tensors. For them the weight/bias-gradient partials live in this file-scope array instead of a
+// caller-provided workspace. It is 2 MiB (512 Ki floats); every GPU that loads the library keeps it
+// until the process exits. Host code must not pass the symbol itself to a kernel (on the host it is
+// only a stand-in): its device address is looked up once per device with cudaGetSymbolAddress.
+constexpr int64_t kLnNoAllocScratchFloats = 512 * 1024;
+static __device__ __align__(256) float g_ln_noalloc_scratch[kLnNoAllocScratchFloats];
+
+std::mutex g_ln_noalloc_mu;
+void* g_ln_noalloc_ptr[256];  // per device ordinal
+
+// Device address of g_ln_noalloc_scratch on the current device (resolved on first use).
+int ln_noalloc_scratch(float** out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "layernorm_bwd_noalloc: cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 256) return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> g(g_ln_noalloc_mu);
+  if (!g_ln_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (int rc = check_cuda(cudaGetSymbolAddress(&p, g_ln_noalloc_scratch), "layernorm_bwd_noalloc: cudaGetSymbolAddress"))
+      return rc;
+    g_ln_noalloc_ptr[dev] = p;
+  }
+  *out = (float*)g_ln_noalloc_ptr[dev];
+  return 0;
+}
+
+// The LayerNorm backward launch sequence for an explicit plan whose partial slots fit `part`.
+template <typename T>
+int ln_bwd_planned(const b2_layernorm_args* a, const LnPlan& p, float* part, cudaStream_t st) {
+  constexpr int VV = sizeof(T) == 4 ? 4 : 8;
+  const bool want_w = a->dw || a->db;
+  float* pw = want_w ? part : nullptr;
+  {
+    LaunchScope ls("layernorm_bwd_noalloc", st);
+    if (p.kind == 0) {
+      if (p.v == 1)
+        ln_reg_switch<T, 1>(a, p, st, false, pw);
+      else
+        ln_reg_switch<T, VV>(a, p, st, false, pw);
+    } else {
+      if (a->dx)
+        ln_bwd_long<T><<<p.grid, 256, 0, st>>>((const T*)a->x, (const T*)a->w, (const T*)a->g, a->mean, a->rstd,
+                                               (T*)a->dx, a->rows, a->D);
+      if (want_w) {
+        int64_t rps = (a->rows + p.nslots - 1) / p.nslots;
+        dim3 grid((unsigned)((a->D + 255) / 256), (unsigned)p.nslots);
+        ln_wgrad_part_long<T><<<grid, 256, 0, st>>>((const T*)a->x, (const T*)a->g, a->mean, a->rstd, pw, a->rows, a->D,
+                                                     rps);
+      }
+    }
+  }
+  if (want_w) {
+    LaunchScope ls("layernorm_wgrad_reduce_noalloc", st);
+    dim3 block(32, 8);
+    ln_wgrad_reduce<T><<<(unsigned)((a->D + 31) / 32), block, 0, st>>>(pw, p.nslots, a->D, (T*)a->dw, (T*)a->db);
+  }
+  return after_launch("b2_layernorm_bwd_noalloc");
+}
+
 }  // namespace
 }  // namespace b2
 
@@ -708,6 +773,39 @@ int b2_softmax_fwd(const b2_softmax_args* a, b2_stream_t s) { return softmax_ent
 int b2_softmax_bwd(const b2_softmax_args* a, b2_stream_t s) { return softmax_entry(a, s, false); }
 int b2_layernorm_fwd(const b2_layernorm_args* a, b2_stream_t s) { return ln_entry(a, s, true); }
 int b2_layernorm_bwd(const b2_layernorm_args* a, b2_stream_t s) { return ln_entry(a, s, false); }
+int b2_layernorm_bwd_noalloc(const b2_layernorm_args* a, b2_stream_t stream) {
+  if (!a) return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: null args");
+  if (int rc = ensure_init()) return rc;
+  if (a->rows < 0 || a->D < 0) return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: negative size");
+  if (a->rows == 0 || a->D == 0) return 0;
+  if (!a->x || !a->mean || !a->rstd || !a->g) return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: null pointer");
+  // each partial slot holds 2*D floats (weight and bias columns); at least one slot must fit
+  const int64_t max_slots = kLnNoAllocScratchFloats / (2 * a->D);
+  if ((a->dw || a->db) && max_slots < 1)
+    return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: D = " + std::to_string(a->D) + " exceeds the static scratch (D <= " +
+                                std::to_string(kLnNoAllocScratchFloats / 2) + ")");
+  LnPlan p = ln_plan(a);
+  if (a->dw || a->db) {
+    if (p.kind == 0) {
+      const int rpb = 256 / p.group;
+      if (max_slots < rpb)
+        return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: D too large for the static scratch with this row layout");
+      if ((int64_t)p.grid * rpb > max_slots) p.grid = (int)(max_slots / rpb);
+      p.nslots = (int64_t)p.grid * rpb;
+    } else if (p.nslots > max_slots) {
+      p.nslots = max_slots;
+    }
+  }
+  float* part = nullptr;
+  if (int rc = ln_noalloc_scratch(&part)) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (a->dtype) {
+    case B2_F32: return ln_bwd_planned<float>(a, p, part, st);
+    case B2_BF16: return ln_bwd_planned<__nv_bfloat16>(a, p, part, st);
+    case B2_F16: return ln_bwd_planned<__half>(a, p, part, st);
+    default: return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: dtype must be F32, BF16 or F16");
+  }
+}
 uint64_t b2_layernorm_bwd_workspace_bytes(const b2_layernorm_args* a) {
   if (!a || a->rows <= 0 || a->D <= 0) return 0;
   if (ensure_init()) return 0;
