@@ -66,7 +66,7 @@ bool make_tmap(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* bas
 
 namespace {
 
-constexpr int BM = 128, BK = 64;
+constexpr int BM = 128, BK = 64;  // one UMMA M-tile; a CTA tile stacks MSUB of them
 
 struct TcParams {
   int64_t M, N, K, batch;
@@ -87,16 +87,22 @@ struct TcParams {
   int64_t deq_rows;   // rows of q (output features N of the linear)
 };
 
-template <int BN, int DEQ>
+template <int BN, int DEQ, int MSUB>
 struct Cfg {
-  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int BMT = BM * MSUB;             // rows of the CTA tile
+  static constexpr int A_BYTES = BMT * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int R_BYTES = DEQ ? BN * BK : 0;  // raw int8 tile
   static constexpr int STAGE = A_BYTES + B_BYTES + R_BYTES;
   static constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
-  static constexpr int THREADS = DEQ ? 320 : 192;
+  static constexpr int DEQ_WARPS = DEQ ? 8 : 0;
+  static constexpr int THREADS = (6 + DEQ_WARPS) * 32;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t SUB_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per M sub-tile
+  static constexpr uint32_t ACC_COLS = MSUB * SUB_COLS;  // one accumulator (all M sub-tiles)
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;    // double-buffered (a power of two)
+  static_assert(TMEM_COLS <= 512, "accumulators exceed TMEM");
+  static_assert(BN % 16 == 0 && BN <= 256, "UMMA N must be a multiple of 16 up to 256");
 };
 
 __device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
@@ -108,19 +114,45 @@ __device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <int BN, bool BF16, int DEQ>
-__global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
+// 4 int8 (one 32-bit word) -> 4 exact fp32: bias to unsigned, splice the byte under the exponent of
+// 2^23 with a byte permute, subtract 2^23 + 128 (exact).
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* f) {
+  w ^= 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540)) - 8388736.f;
+  f[1] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541)) - 8388736.f;
+  f[2] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542)) - 8388736.f;
+  f[3] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543)) - 8388736.f;
+}
+
+// 16 int8 * scale -> 8 words of packed bf16 (one fp32 multiply and one round-to-nearest-even each,
+// the same bits as b2_dequant_int8 for every finite product).
+__device__ __forceinline__ void dequant16(const int4& raw, float s, uint32_t* w) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float f[4];
+    i8x4_to_f32(r[i], f);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(f[0] * s, f[1] * s);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(f[2] * s, f[3] * s);
+    w[2 * i] = *reinterpret_cast<uint32_t*>(&lo);
+    w[2 * i + 1] = *reinterpret_cast<uint32_t*>(&hi);
+  }
+}
+
+template <int BN, bool BF16, int DEQ, int MSUB>
+__global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
-  using C = Cfg<BN, DEQ>;
+  using C = Cfg<BN, DEQ, MSUB>;
   constexpr int S = C::STAGES;
+  constexpr int NDQ = C::DEQ_WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::STAGE);
-  uint64_t* full = bars;            // [S]  TMA landed
-  uint64_t* empty = bars + S;       // [S]  MMA done reading the stage
-  uint64_t* tfull = bars + 2 * S;   // [2]  accumulator ready
-  uint64_t* tempty = bars + 2 * S + 2;  // [2] accumulator drained
-  uint64_t* bready = bars + 2 * S + 4;  // [S] (int8) B stage dequantised
+  uint64_t* full = bars;                // [S]  TMA landed
+  uint64_t* empty = bars + S;           // [S]  MMA done reading the stage
+  uint64_t* tfull = bars + 2 * S;       // [2]  accumulator ready
+  uint64_t* tempty = bars + 2 * S + 2;  // [2]  accumulator drained
+  uint64_t* bready = bars + 2 * S + 4;  // [S]  (int8) B stage dequantised
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -131,7 +163,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
     for (int i = 0; i < S; ++i) {
       tc::mbar_init(&full[i], 1);
       tc::mbar_init(&empty[i], 1);
-      tc::mbar_init(&bready[i], 128);
+      tc::mbar_init(&bready[i], NDQ > 0 ? NDQ : 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&tfull[i], 1);
@@ -154,7 +186,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
     b = t / per_b;
     int r = t - b * per_b;
     int mt = r % p.m_tiles, nt = r / p.m_tiles;
-    m0 = mt * BM;
+    m0 = mt * C::BMT;
     n0 = nt * BN;
   };
 
@@ -182,12 +214,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
           const uint32_t bytes = C::A_BYTES + (DEQ ? C::R_BYTES : C::B_BYTES);
           tc::mbar_arrive_expect_tx(&full[stage], bytes);
           const int k0 = kb * BK;
-          if (!p.a_mn) {
+          if (!p.a_mn) {  // one box of BMT rows x 64 k
             if (p.a3d) tc::tma_load_3d(sa, &tmA, &full[stage], k0, m0, b);
             else tc::tma_load_2d(sa, &tmA, &full[stage], k0, m0);
-          } else {
+          } else {  // BMT/64 boxes of 64 m x 64 k
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) {
+            for (int j = 0; j < C::BMT / 64; ++j) {
               if (p.a3d) tc::tma_load_3d(sa + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0, b);
               else tc::tma_load_2d(sa + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
             }
@@ -236,7 +268,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
           break;
         }
         tc::tc_fence_after();
-        const uint32_t d = tbase + (uint32_t)(acc * BN);
+        const uint32_t d = tbase + (uint32_t)(acc * C::ACC_COLS);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, p.err) || (DEQ && !tc::mbar_wait(&bready[stage], phase, p.err))) {
             ok = false;
@@ -250,9 +282,15 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
           for (int k = 0; k < BK / 16; ++k) {
             // K-major: +32 B per 16-element K step inside the 128 B swizzle row.
             // MN-major: +16 rows of 128 B per step; LBO = distance between 64-element MN chunks.
-            uint64_t ad = p.a_mn ? tc::sdesc_sw128(a_addr + k * 2048, 8192, 1024) : tc::sdesc_sw128(a_addr + k * 32, 16, 1024);
-            uint64_t bd = p.b_mn ? tc::sdesc_sw128(b_addr + k * 2048, 8192, 1024) : tc::sdesc_sw128(b_addr + k * 32, 16, 1024);
-            tc::mma_f16_ss(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            const uint64_t bd = p.b_mn ? tc::sdesc_sw128(b_addr + k * 2048, 8192, 1024)
+                                       : tc::sdesc_sw128(b_addr + k * 32, 16, 1024);
+#pragma unroll
+            for (int ms = 0; ms < MSUB; ++ms) {
+              // M sub-tile ms: K-major rows 128*ms.. at +ms*16 KB; MN-major chunks 2ms, 2ms+1 at +ms*16 KB
+              const uint64_t ad = p.a_mn ? tc::sdesc_sw128(a_addr + ms * 16384 + k * 2048, 8192, 1024)
+                                         : tc::sdesc_sw128(a_addr + ms * 16384 + k * 32, 16, 1024);
+              tc::mma_f16_ss(d + ms * C::SUB_COLS, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           tc::mma_commit(&empty[stage]);
           if (++stage == S) {
@@ -268,8 +306,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
   } else if (warp < 6) {
     // ------------------------------- epilogue -----------------------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
     int it = 0;
+    using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       if (!tc::mbar_wait(&tfull[acc], (it >> 1) & 1, p.err) || *abort_flag) {
@@ -279,38 +317,40 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
       tc::tc_fence_after();
       int m0, n0, b;
       tile_coords(t, m0, n0, b);
-      const int64_t row = m0 + row_in_tile;
-      const bool row_ok = row < p.M;
-      using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      OutT* crow = (OutT*)p.c + b * p.c_sb + row * p.c_sm;
-      const OutT* brow = (const OutT*)p.bias + b * p.bias_sb + row * p.bias_sm;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t r[32];
-        __syncwarp();
-        tc::tmem_ld32(tbase + (uint32_t)(acc * BN + ch * 32) + ((uint32_t)(q * 32) << 16), r);
-        tc::tmem_wait_ld();
-        const int64_t col0 = n0 + ch * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        float v[32];
+      for (int ms = 0; ms < MSUB; ++ms) {
+        const int64_t row = m0 + ms * BM + q * 32 + lane;
+        const bool row_ok = row < p.M;
+        OutT* crow = (OutT*)p.c + b * p.c_sb + row * p.c_sm;
+        const OutT* brow = (const OutT*)p.bias + b * p.bias_sb + row * p.bias_sm;
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          uint32_t r[32];
+          __syncwarp();
+          tc::tmem_ld32(tbase + (uint32_t)(acc * C::ACC_COLS + ms * C::SUB_COLS + ch * 32) + ((uint32_t)(q * 32) << 16), r);
+          tc::tmem_wait_ld();
+          const int64_t col0 = n0 + ch * 32;
+          if (!row_ok || col0 >= p.N) continue;
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
-        if (p.has_bias) {
+          for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+          if (p.has_bias) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) v[j] += p.beta * to_f32(brow[(col0 + j) * p.bias_sn]);
-        }
-        const bool vec = (p.c_sn == 1) && (col0 + 32 <= p.N) && ((reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0);
-        if (vec) {
-          uint4* dst = reinterpret_cast<uint4*>(crow + col0);
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) v[j] += p.beta * to_f32(brow[(col0 + j) * p.bias_sn]);
+          }
+          const bool vec = (p.c_sn == 1) && (col0 + 32 <= p.N) && ((reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0);
+          if (vec) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + col0);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            dst[j] = make_uint4(pack_out(v[8 * j], v[8 * j + 1], BF16), pack_out(v[8 * j + 2], v[8 * j + 3], BF16),
-                                pack_out(v[8 * j + 4], v[8 * j + 5], BF16), pack_out(v[8 * j + 6], v[8 * j + 7], BF16));
-        } else {
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(pack_out(v[8 * j], v[8 * j + 1], BF16), pack_out(v[8 * j + 2], v[8 * j + 3], BF16),
+                                  pack_out(v[8 * j + 4], v[8 * j + 5], BF16), pack_out(v[8 * j + 6], v[8 * j + 7], BF16));
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) crow[(col0 + j) * p.c_sn] = from_f32<OutT>(v[j]);
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.N) crow[(col0 + j) * p.c_sn] = from_f32<OutT>(v[j]);
+          }
         }
       }
       tc::tc_fence_before();
@@ -318,7 +358,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
     }
   } else if (DEQ) {
     // ------------------------------- int8 dequant -------------------------------------------
-    const int dt = threadIdx.x - 6 * 32;  // 0..127
+    const int dt = threadIdx.x - 6 * 32;  // 0 .. NDQ-1
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
@@ -335,7 +375,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
         if (!p.b_mn) {
           // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
-          for (int i = dt; i < BN * 4; i += 128) {
+          for (int i = dt; i < BN * 4; i += NDQ) {
             const int n = i >> 2, j = i & 3;  // 16 int8 = k 16j..16j+15
             const int64_t gn = (int64_t)n0 + n;
             float s = 0.f;
@@ -343,13 +383,9 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
               s = p.scale_layout == 0
                       ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
                       : reinterpret_cast<const float*>(p.scale)[gn];
-            int4 raw = *reinterpret_cast<const int4*>(sr + n * 64 + j * 16);
-            const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+            const int4 raw = *reinterpret_cast<const int4*>(sr + n * 64 + j * 16);
             uint32_t w[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              w[e] = (uint32_t)f32_to_bf16_bits((float)qb[2 * e] * s) |
-                     ((uint32_t)f32_to_bf16_bits((float)qb[2 * e + 1] * s) << 16);
+            dequant16(raw, s, w);
             uint8_t* rowp = sb + n * 128;
             const int c0 = 2 * j, c1 = 2 * j + 1;
             *reinterpret_cast<uint4*>(rowp + ((c0 ^ (n & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -358,7 +394,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
         } else {
           // backward: raw [64 rows i (n_feat)][BN bytes (k_feat = n_gemm)]; B stage MN-major SW128:
           // chunk j = n_gemm/64 at j*8192, row i at i*128, 16 B granule g at ((g ^ (i & 7)) * 16).
-          for (int e = dt; e < 64 * (BN / 16); e += 128) {
+          for (int e = dt; e < 64 * (BN / 16); e += NDQ) {
             const int i = e / (BN / 16), qd = e % (BN / 16);
             const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
             const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
@@ -367,13 +403,9 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
               s = p.scale_layout == 0
                       ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
                       : reinterpret_cast<const float*>(p.scale)[nf];
-            int4 raw = *reinterpret_cast<const int4*>(sr + i * BN + qd * 16);
-            const int8_t* qb = reinterpret_cast<const int8_t*>(&raw);
+            const int4 raw = *reinterpret_cast<const int4*>(sr + i * BN + qd * 16);
             uint32_t w[8];
-#pragma unroll
-            for (int x = 0; x < 8; ++x)
-              w[x] = (uint32_t)f32_to_bf16_bits((float)qb[2 * x] * s) |
-                     ((uint32_t)f32_to_bf16_bits((float)qb[2 * x + 1] * s) << 16);
+            dequant16(raw, s, w);
             const int chunk = (qd * 16) >> 6, g0 = ((qd * 16) & 63) >> 3;
             uint8_t* rowp = sb + chunk * 8192 + i * 128;
             *reinterpret_cast<uint4*>(rowp + ((g0 ^ (i & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -404,13 +436,13 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ>::THREADS, 1)
 
 bool tma_ok_stride(int64_t s_elems, int esz) { return ((s_elems * esz) % 16) == 0; }
 
-template <int BN, bool BF16, int DEQ>
+template <int BN, bool BF16, int DEQ, int MSUB>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t st, const char* name) {
-  using C = Cfg<BN, DEQ>;
+  using C = Cfg<BN, DEQ, MSUB>;
   static bool attr_set = false;  // set once per process (single device per process)
   if (!attr_set) {
-    if (int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<BN, BF16, DEQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 C::SMEM),
+    if (int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<BN, BF16, DEQ, MSUB>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                             "cudaFuncSetAttribute(gemm_tc)"))
       return rc;
     attr_set = true;
@@ -418,7 +450,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& 
   int tiles = p.m_tiles * p.n_tiles * (int)p.batch;
   int grid = std::min(tiles, device_info().sm_count);
   LaunchScope ls(name, st);
-  gemm_tc_kernel<BN, BF16, DEQ><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
+  gemm_tc_kernel<BN, BF16, DEQ, MSUB><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
   return after_launch(name);
 }
 
@@ -432,7 +464,8 @@ int pick_bn(int64_t M, int64_t N, int64_t batch) {
     double work = (double)waves * sms * BM * bn;
     return useful / work * tile_eff;
   };
-  return score(256, 1.0) >= score(128, 0.92) ? 256 : 128;
+  // 128-wide tiles need 1.5x the operand bandwidth per FLOP of 256-wide ones (measured: ~0.65x the rate)
+  return score(256, 1.0) >= score(128, 0.65) ? 256 : 128;
 }
 
 }  // namespace
@@ -512,8 +545,10 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
       return fail(B2_ERR_ARG, "gemm_tc: tensor map for B rejected");
   }
   if (BN == 256)
-    return bf16 ? launch_kernel<256, true, 0>(ta, tb, p, st, "gemm_tc_bn256") : launch_kernel<256, false, 0>(ta, tb, p, st, "gemm_tc_bn256");
-  return bf16 ? launch_kernel<128, true, 0>(ta, tb, p, st, "gemm_tc_bn128") : launch_kernel<128, false, 0>(ta, tb, p, st, "gemm_tc_bn128");
+    return bf16 ? launch_kernel<256, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn256")
+                : launch_kernel<256, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn256");
+  return bf16 ? launch_kernel<128, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn128")
+              : launch_kernel<128, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn128");
 }
 
 }  // namespace b2
@@ -536,10 +571,27 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
     return fail(B2_ERR_ARG, "int8_gemm: x and q must be 16-byte aligned, x_ld a multiple of 8 and K of 16");
   if (a->transpose_w && a->bias) return fail(B2_ERR_ARG, "int8_gemm: bias is only supported in the forward form");
   cudaStream_t st = (cudaStream_t)stream;
-  constexpr int BN = 256;  // a wide W tile amortises the dequant over more of the M tile
+  // Tile choice. The dequant work per FLOP is 1/(2*rows of the CTA tile), so two stacked M=128 UMMA
+  // tiles (256 rows) halve it; among the shapes the kernel supports, take the one with the best
+  // wave-quantised SM utilisation, weighted by how well the dequant warps keep up.
+  struct Choice { int bn, msub; double eff; };
+  const Choice fwd_opts[] = {{128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const Choice dx_opts[] = {{128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
+  Choice best{0, 0, -1.0};
+  double best_score = -1.0;
+  const int nopts = a->transpose_w ? 3 : 4;
+  for (int i = 0; i < nopts; ++i) {
+    const Choice c = a->transpose_w ? dx_opts[i] : fwd_opts[i];
+    const int64_t tiles = ((a->M + 128 * c.msub - 1) / (128 * c.msub)) * ((out_cols + c.bn - 1) / c.bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double score = (double)a->M * out_cols / ((double)waves * sms * 128 * c.msub * c.bn) * c.eff;
+    if (score > best_score) best_score = score, best = c;
+  }
+  const int BN = best.bn, BMT = 128 * best.msub;
   TcParams p{};
   p.M = a->M, p.N = out_cols, p.K = red, p.batch = 1;
-  p.m_tiles = (int)((a->M + BM - 1) / BM);
+  p.m_tiles = (int)((a->M + BMT - 1) / BMT);
   p.n_tiles = (int)((out_cols + BN - 1) / BN);
   p.k_blocks = (int)((red + BK - 1) / BK);
   p.a_mn = 0;
@@ -552,17 +604,21 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   CUtensorMap ta, tb;
   {
     uint64_t dims[2] = {(uint64_t)red, (uint64_t)a->M}, strides[1] = {(uint64_t)a->x_ld * 2};
-    uint32_t box[2] = {64, BM};
+    uint32_t box[2] = {64, (uint32_t)BMT};
     if (!make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(B2_ERR_ARG, "int8_gemm: tensor map for x rejected");
   }
   {
     uint64_t dims[2] = {(uint64_t)a->K, (uint64_t)a->N}, strides[1] = {(uint64_t)a->K};
     uint32_t box[2];
-    if (!a->transpose_w) box[0] = 64, box[1] = BN;
-    else box[0] = BN, box[1] = 64;
+    if (!a->transpose_w) box[0] = 64, box[1] = (uint32_t)BN;
+    else box[0] = (uint32_t)BN, box[1] = 64;
     if (!make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
       return fail(B2_ERR_ARG, "int8_gemm: tensor map for q rejected");
   }
-  return launch_kernel<BN, true, 1>(ta, tb, p, st, a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd");
+  const char* name = a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd";
+  if (best.msub == 2 && BN == 128) return launch_kernel<128, true, 1, 2>(ta, tb, p, st, name);
+  if (best.msub == 2 && BN == 96) return launch_kernel<96, true, 1, 2>(ta, tb, p, st, name);
+  if (BN == 256) return launch_kernel<256, true, 1, 1>(ta, tb, p, st, name);
+  return launch_kernel<128, true, 1, 1>(ta, tb, p, st, name);
 }
