@@ -60,6 +60,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--no-dit", action="store_true")
     return ap.parse_args()
 
 
@@ -294,6 +295,13 @@ def run_ours(args, rank, world, local_rank):
     extra = None
     if rank == 0 and not args.no_extra:
         extra = run_extra(tv, dev, flush, peaks)
+    if not args.no_dit:
+        dit = {}
+        if world == 1:
+            dit["config3_block"] = run_dit(dev, world, blocks=1, tokens=1024, steps=10, warmup=3)
+        dit["config4_stack"] = run_dit(dev, world, blocks=28, tokens=4096, steps=5, warmup=2)
+        if rank == 0:
+            extra = dict(extra or {}, dit_lora_step=dit)
 
     result = {"metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": K,
               "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max, 5), "higher_is_better": True,
@@ -305,6 +313,42 @@ def run_ours(args, rank, world, local_rank):
     if extra:
         result["extra"] = extra
     return result
+
+
+def run_dit(dev, world, blocks, tokens, steps, warmup):
+    """DiT LoRA training step: one sample per GPU, LoRA gradients
+    averaged across ranks with bucketed NCCL all-reduce overlapped with the backward; ms/step is the max
+    over ranks of the CUDA-event step time."""
+    from torch_vulkan_b200.dit import DiTStack, LoRATrainer, block_flops, synthetic_batch
+
+    rank = dist.get_rank() if world > 1 else 0
+    model = DiTStack(blocks=blocks, seed=0, device=dev)  # identical replicas on every rank
+    trainer = LoRATrainer(model, lr=1e-4)
+    batch = synthetic_batch(tokens=tokens, seed=1000 + rank, device=dev)  # each rank its own sample
+    for _ in range(warmup):
+        trainer.step(*batch)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = trainer.step(*batch)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    f_fwd, f_bwd = block_flops(tokens=tokens)
+    step_flops = blocks * (f_fwd + f_bwd) * world
+    out = {"blocks": blocks, "tokens": tokens, "samples_per_step": world, "ms_per_step": round(ms, 3),
+           "samples_per_s": round(world / (ms * 1e-3), 2), "tflops": round(step_flops / (ms * 1e-3) / 1e12, 1),
+           "loss": float(loss.item()), "lora_params": sum(p.numel() for p in trainer.params),
+           "allreduce": "bucketed per block, NCCL AVG, overlapped with backward" if world > 1 else None}
+    del trainer, model
+    torch.cuda.empty_cache()
+    return out
 
 
 def timed(fn, flush, iters=50, warm=5):

@@ -1,0 +1,156 @@
+"""Synthetic DiT block with LoRA on frozen int8 base weights — the training workload of BASELINE configs[3]
+(one block, 1024 image tokens) and configs[4] (a 28-block stack at 4096 tokens, data-parallel).
+
+Built from the BASELINE description (the Anima model code of the reference's sd-scripts fork is not part of
+the reference repository): hidden 2048, 16 heads x 128, self-attention + cross-attention to 512 text tokens
+of width 1024, GELU MLP 2048 -> 8192 -> 2048, adaLN-modulated (affine-free) LayerNorm, LoRA rank 16 /
+alpha 16 on the q/k/v/o linears of both attentions (the module layout of tests/anima_on_vk.py:43-48 of the
+reference), every base linear frozen as int8 with a per-output-row fp32 scale. The hot operators run on
+this package's kernels: int8 linears on the fused dequant GEMM (`b2::int8_linear_fwd/dx`), LoRA projections
+on `mm/addmm`, attention on the fused tcgen05 SDPA, LayerNorm on the row kernels, AdamW(foreach=False) on
+`addcmul_/addcdiv_/lerp_`.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import torch_vulkan_b200 as tv
+
+
+class Int8Linear(nn.Module):
+    """Frozen int8 weight [out, in] with a per-output-row fp32 scale; y = x (W*s)^T + b."""
+
+    def __init__(self, in_f, out_f, bias=True, std=0.02, generator=None, device="cuda"):
+        super().__init__()
+        # random init std 0.02, quantised per output row (the set-up runs on the device; it is not timed)
+        w = torch.randn(out_f, in_f, generator=generator, device=generator.device if generator else device) * std
+        w = w.to(device)
+        scale = w.abs().amax(1).clamp_min(1e-8) / 127.0
+        q = torch.round(w / scale[:, None]).clamp_(-127, 127).to(torch.int8)
+        del w
+        self.register_buffer("q", q)
+        self.register_buffer("scale", scale.float())
+        self.register_buffer("bias", torch.zeros(out_f, dtype=torch.bfloat16, device=device) if bias else None)
+
+    def forward(self, x):
+        return tv.int8_linear(x, self.q, self.scale, self.bias)
+
+
+class LoRAInt8Linear(nn.Module):
+    """Frozen int8 base + trainable LoRA: y = base(x) + (x A^T) B^T * alpha / r."""
+
+    def __init__(self, in_f, out_f, rank=16, alpha=16.0, generator=None, device="cuda", dtype=torch.bfloat16):
+        super().__init__()
+        self.base = Int8Linear(in_f, out_f, bias=True, generator=generator, device=device)
+        gdev = generator.device if generator else device
+        self.lora_down = nn.Parameter((torch.randn(rank, in_f, generator=generator, device=gdev) / math.sqrt(in_f)).to(dtype).to(device))
+        # non-zero up-projection so the LoRA path carries gradient and signal from the first step
+        self.lora_up = nn.Parameter((torch.randn(out_f, rank, generator=generator, device=gdev) * 0.02).to(dtype).to(device))
+        self.scale = alpha / rank
+
+    def forward(self, x):
+        y = self.base(x)
+        return y + F.linear(F.linear(x, self.lora_down), self.lora_up) * self.scale
+
+
+class DiTBlock(nn.Module):
+    def __init__(self, hidden=2048, heads=16, text_dim=1024, mlp=8192, rank=16, alpha=16.0, seed=0, device="cuda"):
+        super().__init__()
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.h, self.heads, self.d = hidden, heads, hidden // heads
+        mk = lambda i, o: LoRAInt8Linear(i, o, rank, alpha, generator=g, device=device)  # noqa: E731
+        self.q, self.k, self.v, self.o = mk(hidden, hidden), mk(hidden, hidden), mk(hidden, hidden), mk(hidden, hidden)
+        self.cq, self.ck, self.cv, self.co = mk(hidden, hidden), mk(text_dim, hidden), mk(text_dim, hidden), mk(hidden, hidden)
+        self.fc1 = Int8Linear(hidden, mlp, generator=g, device=device)
+        self.fc2 = Int8Linear(mlp, hidden, generator=g, device=device)
+        # adaLN modulation: (shift, scale, gate) for self-attn, cross-attn and MLP from the conditioning vector
+        self.ada = Int8Linear(hidden, 9 * hidden, generator=g, device=device)
+
+    def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op):
+        B, S, _ = xq.shape
+        Skv = xkv_k.shape[1]
+        q = qp(xq).view(B, S, self.heads, self.d).transpose(1, 2)
+        k = kp(xkv_k).view(B, Skv, self.heads, self.d).transpose(1, 2)
+        v = vp(xkv_v).view(B, Skv, self.heads, self.d).transpose(1, 2)
+        o = F.scaled_dot_product_attention(q, k, v)
+        return op(o.transpose(1, 2).reshape(B, S, self.h))
+
+    def forward(self, x, text, cond):
+        mod = self.ada(F.silu(cond)).unsqueeze(1).chunk(9, dim=-1)
+        sh1, sc1, g1, sh2, sc2, g2, sh3, sc3, g3 = mod
+
+        def modln(t, sh, sc):
+            return F.layer_norm(t, (self.h,), eps=1e-6) * (1 + sc) + sh
+
+        h = modln(x, sh1, sc1)
+        x = x + g1 * self._attn(h, h, h, self.q, self.k, self.v, self.o)
+        h = modln(x, sh2, sc2)
+        x = x + g2 * self._attn(h, text, text, self.cq, self.ck, self.cv, self.co)
+        h = modln(x, sh3, sc3)
+        x = x + g3 * self.fc2(F.gelu(self.fc1(h), approximate="tanh"))
+        return x
+
+
+class DiTStack(nn.Module):
+    def __init__(self, blocks=1, seed=0, device="cuda", **kw):
+        super().__init__()
+        self.blocks = nn.ModuleList([DiTBlock(seed=seed + i, device=device, **kw) for i in range(blocks)])
+
+    def forward(self, x, text, cond):
+        for b in self.blocks:
+            x = b(x, text, cond)
+        return x
+
+    def lora_parameters(self):
+        return [p for n, p in self.named_parameters() if "lora_" in n]
+
+
+def synthetic_batch(tokens=1024, text_tokens=512, hidden=2048, text_dim=1024, batch=1, seed=0, device="cuda"):
+    """Latent tokens (64x64 latent, patch 2 -> 1024 tokens at 512 px; 4096 at 1024 px), text embeddings,
+    conditioning vector and a regression target, all seeded N(0, 1) in bf16."""
+    g = torch.Generator().manual_seed(seed)
+    mk = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16).to(device)  # noqa: E731
+    return mk(batch, tokens, hidden), mk(batch, text_tokens, text_dim), mk(batch, hidden), mk(batch, tokens, hidden)
+
+
+def block_flops(tokens=1024, text_tokens=512, hidden=2048, text_dim=1024, mlp=8192, heads=16):
+    """Forward and backward FLOPs of one block (dX only for frozen weights, no dX into the text context,
+    attention backward = 2.5x forward), excluding LoRA and elementwise work."""
+    lin_f = 2 * tokens * hidden * hidden * 6 + 2 * text_tokens * text_dim * hidden * 2 + 2 * tokens * hidden * mlp * 2
+    attn_f = 4 * tokens * tokens * hidden + 4 * tokens * text_tokens * hidden
+    lin_b = 2 * tokens * hidden * hidden * 6 + 2 * tokens * hidden * mlp * 2  # dX of the frozen linears (no text dX)
+    return lin_f + attn_f, lin_b + 2.5 * attn_f
+
+
+def make_optimizer(params, lr=1e-4):
+    """AdamW(foreach=False): the per-tensor addcmul_/addcdiv_/lerp_ path the reference's trainer uses."""
+    return torch.optim.AdamW(params, lr=lr, betas=(0.9, 0.999), weight_decay=0.01, foreach=False)
+
+
+class LoRATrainer:
+    """One LoRA training step of a DiTStack: forward, MSE loss against the target, backward, data-parallel
+    gradient averaging (bucketed per block, overlapped with the backward when torch.distributed is
+    initialised), AdamW(foreach=False) on the LoRA parameters."""
+
+    def __init__(self, model: DiTStack, lr=1e-4):
+        from torch_vulkan_b200.dp import BucketedGradAllReduce
+
+        self.model = model
+        buckets = [[p for n, p in b.named_parameters() if "lora_" in n] for b in model.blocks]
+        self.params = [p for bk in buckets for p in bk]
+        self.reducer = BucketedGradAllReduce(buckets)
+        self.opt = make_optimizer(self.params, lr=lr)
+
+    def step(self, x, text, cond, target):
+        out = self.model(x, text, cond)
+        loss = F.mse_loss(out.float(), target.float())
+        loss.backward()
+        self.reducer.wait()
+        self.opt.step()
+        self.reducer.zero_grad()
+        return loss.detach()
