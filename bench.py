@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--no-dit", action="store_true")
+    ap.add_argument("--case", choices=["attn", "int8", "rows", "dit"], default=None,
+                    help="run a few eager iterations of one workload and exit (the small case for ncu captures)")
+    ap.add_argument("--case-iters", type=int, default=3)
     return ap.parse_args()
 
 
@@ -474,8 +477,53 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_case(name, iters):
+    """A few untimed eager iterations of one workload, without the profiling gate, so that an ncu launch
+    list or a `--set full` capture sees only the kernels of that workload."""
+    import torch_vulkan_b200 as tv
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(0)
+    if name == "attn":
+        q, k, v, do = (t.to(dev) for t in make_inputs())
+        q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
+        fn = lambda: torch.autograd.grad(F.scaled_dot_product_attention(q, k, v), (q, k, v), do)  # noqa: E731
+    elif name == "int8":
+        x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+        qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8).to(dev)
+        s = (torch.rand(6144, generator=g) * 9e-3 + 1e-3).to(dev)
+        bias = (torch.randn(6144, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        fn = lambda: tv.int8_linear(x, qw, s, bias)  # noqa: E731
+    elif name == "rows":
+        xs = (torch.randn(16, 1024, 1024, generator=g) * 2).to(torch.bfloat16).to(dev)
+        gs = torch.randn(16, 1024, 1024, generator=g).to(torch.bfloat16).to(dev)
+        xl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+        wl = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
+        bl = (0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
+        gl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+
+        def fn():
+            ys = torch.softmax(xs, -1)
+            torch.ops.aten._softmax_backward_data(gs, ys, -1, torch.bfloat16)
+            _, mu, rs = torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6)
+            torch.ops.aten.native_layer_norm_backward(gl, xl, (2048,), mu, rs, wl, bl, [True, True, True])
+    else:  # one DiT block LoRA step (configs[3])
+        from torch_vulkan_b200.dit import DiTStack, LoRATrainer, synthetic_batch
+
+        trainer = LoRATrainer(DiTStack(blocks=1, seed=0, device=dev))
+        batch = synthetic_batch(tokens=1024, device=dev)
+        fn = lambda: trainer.step(*batch)  # noqa: E731
+    for _ in range(iters):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "iters": iters, "kernel_counts": tv.kernel_counts()}), flush=True)
+
+
 def main():
     args = parse()
+    if args.case:
+        run_case(args.case, args.case_iters)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

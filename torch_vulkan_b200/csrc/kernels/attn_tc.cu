@@ -236,18 +236,28 @@ __global__ void __launch_bounds__(320, 1)
       tc::tc_fence_after();
       const int64_t rem = p.Sk - (int64_t)j * C::BKV;
       const int valid = rem < C::BKV ? (int)rem : C::BKV;
-      // pass 1: row max, 32 columns at a time (S stays in TMEM; it is re-read in pass 2)
-      float mx = -INFINITY;
+      // pass 1: row max, 32 columns at a time (S stays in TMEM; it is re-read in pass 2). Eight
+      // independent partial maxima keep the dependency chains short.
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t sr[32];
         __syncwarp();
         tc::tmem_ld32(t_s + c * 32 + lane_off, sr);
         tc::tmem_wait_ld();
+        if (valid == C::BKV) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c * 32 + e < valid) mx = fmaxf(mx, __uint_as_float(sr[e]));
+          for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sr[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e < valid) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sr[e]));
+        }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_blk = mx * p.scale_log2;
       // lazy rescale: keep the old max unless the new one is more than 2^8 larger
       const bool need = (m == -INFINITY) || (m_blk > m + 8.f);
@@ -278,22 +288,27 @@ __global__ void __launch_bounds__(320, 1)
       }
       l *= alpha;
       uint8_t* ptile = smem + C::OFF_P + g * C::P_BYTES;
-      float rowsum = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // pass 2: P = exp2(s * scale_log2 - m) as bf16 into the PV A tile
         uint32_t sr[32];
         __syncwarp();
         tc::tmem_ld32(t_s + c * 32 + lane_off, sr);
         tc::tmem_wait_ld();
+        const bool full = (valid == C::BKV);
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 keys
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int i0 = q4 * 8 + 2 * e, c0 = c * 32 + i0;
-            float p0 = c0 < valid ? ex2(__uint_as_float(sr[i0]) * p.scale_log2 - m) : 0.f;
-            float p1 = c0 + 1 < valid ? ex2(__uint_as_float(sr[i0 + 1]) * p.scale_log2 - m) : 0.f;
-            rowsum += p0 + p1;
+            float p0 = ex2(fmaf(__uint_as_float(sr[i0]), p.scale_log2, -m));
+            float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), p.scale_log2, -m));
+            if (!full) {
+              p0 = c0 < valid ? p0 : 0.f;
+              p1 = c0 + 1 < valid ? p1 : 0.f;
+            }
+            rs4[e] += p0 + p1;
             w[e] = pack2(p0, p1, BF16);
           }
           const int gr = c * 4 + q4;
@@ -301,6 +316,7 @@ __global__ void __launch_bounds__(320, 1)
           *reinterpret_cast<uint4*>(row + (((gr & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      const float rowsum = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l += rowsum;
       tc::fence_async_shared();
       tc::tc_fence_before();
@@ -448,14 +464,15 @@ struct BwdCfg {
   static constexpr int QT_BYTES = BQ * D * 2;         // Q or dO tile, 16 KB
   static constexpr int PT_BYTES = BKV * BQ * 2;       // P^T or dS^T tile, 16 KB
   static constexpr int LD_BYTES = BQ * 8;             // (lse*log2e, delta) per query
+  static constexpr int QS = 3;                        // Q / dO / (lse, delta) prefetch depth
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + KV_BYTES;
-  static constexpr int OFF_Q = OFF_V + KV_BYTES;      // 2 stages
-  static constexpr int OFF_DO = OFF_Q + 2 * QT_BYTES; // 2 stages
-  static constexpr int OFF_P = OFF_DO + 2 * QT_BYTES; // 2 buffers
-  static constexpr int OFF_DS = OFF_P + 2 * PT_BYTES; // 2 buffers
-  static constexpr int OFF_LD = OFF_DS + 2 * PT_BYTES; // 2 stages
-  static constexpr int OFF_BAR = OFF_LD + 2 * LD_BYTES;
+  static constexpr int OFF_Q = OFF_V + KV_BYTES;       // QS stages
+  static constexpr int OFF_DO = OFF_Q + QS * QT_BYTES;  // QS stages
+  static constexpr int OFF_P = OFF_DO + QS * QT_BYTES;  // 2 buffers
+  static constexpr int OFF_DS = OFF_P + 2 * PT_BYTES;   // 2 buffers
+  static constexpr int OFF_LD = OFF_DS + 2 * PT_BYTES;  // QS stages
+  static constexpr int OFF_BAR = OFF_LD + QS * LD_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KB shared-memory limit");
   static constexpr int THREADS = 320;
@@ -472,18 +489,19 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  constexpr int QS = C::QS;
   uint64_t* kv_full = bar + 0;
-  uint64_t* q_full = bar + 1;     // [2] Q_i, dO_i, (lse, delta)_i landed
-  uint64_t* q_empty = bar + 3;    // [2] all MMAs reading Q_i / dO_i done
-  uint64_t* sdp_full = bar + 5;   // S^T_i and dP^T_i in TMEM
-  uint64_t* pds_full = bar + 6;   // [2] P^T_i / dS^T_i written (count 256)
-  uint64_t* pds_empty = bar + 8;  // [2] MMAs reading P^T_i / dS^T_i done
-  uint64_t* dq_full = bar + 10;   // dQ^T_i in TMEM
-  uint64_t* dq_empty = bar + 11;  // dQ^T_i drained (count 256)
-  uint64_t* dkv_full = bar + 12;  // final dK, dV in TMEM
-  uint64_t* sdp_empty = bar + 13; // S^T_i / dP^T_i loaded into registers (count 256)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 15);
+  uint64_t* sdp_full = bar + 1;   // S^T_i and dP^T_i in TMEM
+  uint64_t* pds_full = bar + 2;   // [2] P^T_i / dS^T_i written (count 256)
+  uint64_t* pds_empty = bar + 4;  // [2] MMAs reading P^T_i / dS^T_i done
+  uint64_t* dq_full = bar + 6;    // dQ^T_i in TMEM
+  uint64_t* dq_empty = bar + 7;   // dQ^T_i drained (count 256)
+  uint64_t* dkv_full = bar + 8;   // final dK, dV in TMEM
+  uint64_t* sdp_empty = bar + 9;  // S^T_i / dP^T_i loaded into registers (count 256)
+  uint64_t* q_full = bar + 10;    // [QS] Q_i, dO_i, (lse, delta)_i landed
+  uint64_t* q_empty = bar + 10 + QS;  // [QS] all MMAs reading Q_i / dO_i done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10 + 2 * QS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 11 + 2 * QS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = blockIdx.x * C::BKV;
@@ -493,9 +511,11 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < QS; ++i) {
       tc::mbar_init(&q_full[i], 1);
       tc::mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&pds_full[i], 256);
       tc::mbar_init(&pds_empty[i], 1);
     }
@@ -524,11 +544,11 @@ __global__ void __launch_bounds__(320, 1)
         tc::tma_load_4d(smem + C::OFF_K + c * (C::BKV * 128), &tmK, kv_full, c * 64, k0, h, b);
         tc::tma_load_4d(smem + C::OFF_V + c * (C::BKV * 128), &tmV, kv_full, c * 64, k0, h, b);
       }
-      int issued[2] = {0, 0};
+      int issued[QS] = {};
       bool ok = true;
       for (int i = 0; i < ntile; ++i) {
-        const int s = i & 1;
-        if (!tc::mbar_wait(&q_empty[s], ((uint32_t)(i >> 1) & 1) ^ 1, p.err) || *abort_flag) {
+        const int s = i % QS;
+        if (!tc::mbar_wait(&q_empty[s], ((uint32_t)(i / QS) & 1) ^ 1, p.err) || *abort_flag) {
           ok = false;
           break;
         }
@@ -544,7 +564,7 @@ __global__ void __launch_bounds__(320, 1)
       if (!ok) {
         *abort_flag = 1;
         tc::mbar_wait(kv_full, 0, nullptr);
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < QS; ++s)
           if (issued[s]) tc::mbar_wait(&q_full[s], (uint32_t)((issued[s] - 1) & 1), nullptr);
       }
     }
@@ -557,8 +577,8 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K), v_addr = tc::smem_u32(smem + C::OFF_V);
       bool ok = tc::mbar_wait(kv_full, 0, p.err);
       auto issue_sdp = [&](int i) -> bool {
-        const int s = i & 1;
-        if (!tc::mbar_wait(&q_full[s], (uint32_t)((i >> 1) & 1), p.err)) return false;
+        const int s = i % QS;
+        if (!tc::mbar_wait(&q_full[s], (uint32_t)((i / QS) & 1), p.err)) return false;
         tc::tc_fence_after();
         const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES);
         const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES);
@@ -581,7 +601,8 @@ __global__ void __launch_bounds__(320, 1)
       };
       if (ok) ok = issue_sdp(0);
       for (int i = 0; i < ntile && ok; ++i) {
-        const int s = i & 1;
+        const int s = i & 1;         // P^T / dS^T buffer
+        const int qs = i % QS;       // Q / dO stage
         const uint32_t ph = (uint32_t)((i >> 1) & 1);
         // as soon as S^T_i / dP^T_i are in registers, the next tile's scores can go into TMEM
         if (!tc::mbar_wait(sdp_empty, (uint32_t)(i & 1), p.err)) { ok = false; break; }
@@ -589,8 +610,8 @@ __global__ void __launch_bounds__(320, 1)
         if (i + 1 < ntile && !issue_sdp(i + 1)) { ok = false; break; }
         if (!tc::mbar_wait(&pds_full[s], ph, p.err)) { ok = false; break; }
         tc::tc_fence_after();
-        const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES);
-        const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES);
+        const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + qs * C::QT_BYTES);
+        const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + qs * C::QT_BYTES);
         const uint32_t pt_addr = tc::smem_u32(smem + C::OFF_P + s * C::PT_BYTES);
         const uint32_t ds_addr = tc::smem_u32(smem + C::OFF_DS + s * C::PT_BYTES);
         // dV += P^T dO ; dK += dS^T Q   (M = 128 keys, N = D, K = 64 queries)
@@ -602,7 +623,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int k = 0; k < C::BQ / 16; ++k)
           tc::mma_f16_ss(tbase + C::T_DK, tc::sdesc_sw128(ds_addr + k * 32, 16, 1024),
                          tc::sdesc_sw128(q_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
-        tc::mma_commit(&q_empty[s]);
+        tc::mma_commit(&q_empty[qs]);
         // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
         if (i > 0 && !tc::mbar_wait(dq_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
         tc::tc_fence_after();
@@ -642,8 +663,8 @@ __global__ void __launch_bounds__(320, 1)
       return true;
     };
     for (int i = 0; i < ntile; ++i) {
-      const int s = i & 1;
-      if (!tc::mbar_wait(sdp_full, (uint32_t)(i & 1), p.err) || !tc::mbar_wait(&q_full[s], (uint32_t)((i >> 1) & 1), p.err) ||
+      const int s = i & 1, qs = i % QS;
+      if (!tc::mbar_wait(sdp_full, (uint32_t)(i & 1), p.err) || !tc::mbar_wait(&q_full[qs], (uint32_t)((i / QS) & 1), p.err) ||
           *abort_flag) {
         ok = false;
         break;
@@ -658,7 +679,7 @@ __global__ void __launch_bounds__(320, 1)
       tc::mbar_arrive(sdp_empty);
       // P^T / dS^T buffer s was last read by the MMAs of tile i-2
       if (i >= 2 && !tc::mbar_wait(&pds_empty[s], (uint32_t)(((i - 2) >> 1) & 1), p.err)) { ok = false; break; }
-      const float2* ld = reinterpret_cast<const float2*>(smem + C::OFF_LD + s * C::LD_BYTES) + g * 32;
+      const float2* ld = reinterpret_cast<const float2*>(smem + C::OFF_LD + qs * C::LD_BYTES) + g * 32;
       uint8_t* pt = smem + C::OFF_P + s * C::PT_BYTES + r * 128;
       uint8_t* dst = smem + C::OFF_DS + s * C::PT_BYTES + r * 128;
 #pragma unroll
