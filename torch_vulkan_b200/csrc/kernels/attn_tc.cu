@@ -46,15 +46,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool bf16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Writes 8 packed pairs (16 elements) of row `r` into a K-major 128B-swizzled tile whose rows hold
-// 64 elements: granules g0, g0+1 of chunk `chunk` (chunk stride `chunk_bytes`).
-__device__ __forceinline__ void st_sw128_pair(uint8_t* tile, int chunk, int chunk_bytes, int r, int g0,
-                                              const uint32_t* w) {
-  uint8_t* row = tile + chunk * chunk_bytes + r * 128;
-  *reinterpret_cast<uint4*>(row + (((g0) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-  *reinterpret_cast<uint4*>(row + (((g0 + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
-}
-
 struct AttnTcParams {
   int64_t B, H, Sq, Sk;
   float scale_log2;  // scale * log2(e)
@@ -110,8 +101,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* s_full = bar + 9;   // [2] S of block j into S[j&1]
   uint64_t* p_full = bar + 11;  // [2] P of block j into P[j&1] (count 128)
   uint64_t* o_upd = bar + 13;   // [2] PV of block j into O[j&1] done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 15);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 16);
+  uint64_t* s_free = bar + 15;  // [2] S[j&1] of block j read into registers (count 128)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 18);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * C::BQ;
@@ -129,10 +121,14 @@ __global__ void __launch_bounds__(320, 1)
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 128);
       tc::mbar_init(&o_upd[i], 1);
+      tc::mbar_init(&s_free[i], 128);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
+  // the previous kernel on the stream must be done before any global or tensor memory is touched;
+  // TMEM is allocated only after this wait, so a waiting CTA never holds columns another CTA needs
+  tc::pdl_wait();
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
     tc::tmem_relinquish();
@@ -141,28 +137,36 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  tc::pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: Q once, then K_j / V_j into 2-stage rings ----------------
+      // ---------------- producer: Q, K_0, K_1, then V_j followed by K_j+2 ----------------
+      // (the order in which the MMA warp consumes them: S_j+2 is issued before PV_j)
       bool ok = true;
       tc::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
       for (int c = 0; c < C::DCH; ++c) tc::tma_load_4d(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, q_full, c * 64, q0, h, b);
       int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};
-      for (int j = 0; j < nblk && ok; ++j) {
+      auto load_k = [&](int j) -> bool {
         const int s = j & 1;
-        const uint32_t ph = (uint32_t)((j >> 1) & 1);
-        if (!tc::mbar_wait(&k_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
+        if (!tc::mbar_wait(&k_empty[s], (uint32_t)(((j >> 1) & 1) ^ 1), p.err) || *abort_flag) return false;
         tc::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
         for (int c = 0; c < C::DCH; ++c)
           tc::tma_load_4d(smem + C::OFF_K + s * C::K_BYTES + c * (C::BKV * 128), &tmK, &k_full[s], c * 64, j * C::BKV, h, b);
         issued_k[s]++;
-        if (!tc::mbar_wait(&v_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!tc::mbar_wait(&v_empty[s], (uint32_t)(((j >> 1) & 1) ^ 1), p.err) || *abort_flag) return false;
         tc::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
         for (int c = 0; c < C::DCH; ++c)
           tc::tma_load_4d(smem + C::OFF_V + s * C::V_BYTES + c * (C::BKV * 128), &tmV, &v_full[s], c * 64, j * C::BKV, h, b);
         issued_v[s]++;
-      }
+        return true;
+      };
+      ok = load_k(0) && (nblk < 2 || load_k(1));
+      for (int j = 0; j < nblk && ok; ++j) ok = load_v(j) && (j + 2 >= nblk || load_k(j + 2));
       if (!ok) {
         *abort_flag = 1;
         tc::mbar_wait(q_full, 0, nullptr);
@@ -175,6 +179,9 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
+      // For block j: S_j+2 (into the TMEM tile of S_j) as soon as the softmax group has read S_j into
+      // registers, then PV_j once its P tile is in shared memory. S_j+2 thus runs on the tensor cores
+      // while the softmax of S_j is still being computed.
       constexpr uint32_t IDESC_S = tc::idesc_f16(128, C::BKV, BF16, false, false);  // Q K^T: both K-major
       constexpr uint32_t IDESC_O = tc::idesc_f16(128, D, BF16, false, true);        // P V: V is MN-major
       const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q);
@@ -198,6 +205,11 @@ __global__ void __launch_bounds__(320, 1)
       if (ok && nblk > 1) ok = issue_s(1);
       for (int j = 0; j < nblk && ok; ++j) {
         const int s = j & 1;
+        if (j + 2 < nblk) {
+          if (!tc::mbar_wait(&s_free[s], (uint32_t)((j >> 1) & 1), p.err)) { ok = false; break; }
+          tc::tc_fence_after();
+          if (!issue_s(j + 2)) { ok = false; break; }
+        }
         if (!tc::mbar_wait(&p_full[s], (uint32_t)((j >> 1) & 1), p.err) ||
             !tc::mbar_wait(&v_full[s], (uint32_t)((j >> 1) & 1), p.err)) {
           ok = false;
@@ -214,7 +226,6 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc::mma_commit(&o_upd[s]);
         tc::mma_commit(&v_empty[s]);
-        if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
       }
       if (!ok) *abort_flag = 1;
     }
@@ -225,6 +236,7 @@ __global__ void __launch_bounds__(320, 1)
     const int r = quarter * 32 + lane;  // query row inside the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t t_s = tbase + C::T_S + g * 128, t_o = tbase + C::T_O + g * 128;
+    const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     int kb = 0;  // blocks processed by this warpgroup
@@ -234,28 +246,27 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc::tc_fence_after();
+      // the whole 128-column S row in registers; TMEM S goes back to the next S MMA right away
+      uint32_t sr[128];
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(t_s + c * 32 + lane_off, sr + 32 * c);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::reg_fence32(sr + 32 * c);
+      tc::tc_fence_before();
+      tc::mbar_arrive(&s_free[g]);
       const int64_t rem = p.Sk - (int64_t)j * C::BKV;
-      const int valid = rem < C::BKV ? (int)rem : C::BKV;
-      // pass 1: row max, 32 columns at a time (S stays in TMEM; it is re-read in pass 2). Eight
-      // independent partial maxima keep the dependency chains short.
+      if (rem < C::BKV) {  // ragged last block: keys past the end contribute exp2(-inf) = 0
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          if (e >= (int)rem) sr[e] = __float_as_uint(-INFINITY);
+      }
       float mx8[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+      for (int e = 0; e < 8; ++e) mx8[e] = __uint_as_float(sr[e]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        __syncwarp();
-        tc::tmem_ld32(t_s + c * 32 + lane_off, sr);
-        tc::tmem_wait_ld();
-        if (valid == C::BKV) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sr[e]));
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e < valid) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sr[e]));
-        }
-      }
+      for (int e = 8; e < 128; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sr[e]));
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_blk = mx * p.scale_log2;
@@ -267,57 +278,49 @@ __global__ void __launch_bounds__(320, 1)
         alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
         m = m_new;
       }
-      if (kb > 0 && __any_sync(0xffffffffu, need)) {
-        // O[g] holds this group's sum up to its previous block: wait for that PV, then scale in TMEM
+      // PV of this group's previous block must be complete before its P tile is overwritten and
+      // before O is rescaled (it was issued when that P tile was published, so the wait is short)
+      if (kb > 0) {
         if (!tc::mbar_wait(&o_upd[g], (uint32_t)((kb - 1) & 1), p.err)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the S row is still in registers
+            uint32_t orow[16];
+            tc::tmem_ld16(t_o + c * 16 + lane_off, orow);
+            tc::tmem_wait_ld();
+            tc::reg_fence16(orow);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t orow[32];
-          tc::tmem_ld32(t_o + c * 32 + lane_off, orow);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
-          tc::tmem_st16(t_o + c * 32 + lane_off, orow);
-          tc::tmem_st16(t_o + c * 32 + 16 + lane_off, orow + 16);
-        }
-        tc::tmem_wait_st();
-      }
-      l *= alpha;
-      uint8_t* ptile = smem + C::OFF_P + g * C::P_BYTES;
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial row sums
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {  // pass 2: P = exp2(s * scale_log2 - m) as bf16 into the PV A tile
-        uint32_t sr[32];
-        __syncwarp();
-        tc::tmem_ld32(t_s + c * 32 + lane_off, sr);
-        tc::tmem_wait_ld();
-        const bool full = (valid == C::BKV);
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 keys
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i0 = q4 * 8 + 2 * e, c0 = c * 32 + i0;
-            float p0 = ex2(fmaf(__uint_as_float(sr[i0]), p.scale_log2, -m));
-            float p1 = ex2(fmaf(__uint_as_float(sr[i0 + 1]), p.scale_log2, -m));
-            if (!full) {
-              p0 = c0 < valid ? p0 : 0.f;
-              p1 = c0 + 1 < valid ? p1 : 0.f;
-            }
-            rs4[e] += p0 + p1;
-            w[e] = pack2(p0, p1, BF16);
+            for (int e = 0; e < 16; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
+            tc::tmem_st16(t_o + c * 16 + lane_off, orow);
           }
-          const int gr = c * 4 + q4;
-          uint8_t* row = ptile + (gr >> 3) * (128 * 128) + r * 128;
-          *reinterpret_cast<uint4*>(row + (((gr & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          tc::tmem_wait_st();
         }
       }
-      const float rowsum = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-      l += rowsum;
+      // P = exp2(s * scale_log2 - m) as 16-bit pairs, 8 keys (one 16-byte granule) at a time into the
+      // 128-byte swizzled K-major A tile of the PV MMA
+      const float2 nm = make_float2(-m, -m);
+      float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      uint8_t* ptile = smem + C::OFF_P + g * C::P_BYTES;
+#pragma unroll
+      for (int gr = 0; gr < 16; ++gr) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = gr * 8 + 2 * e;
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])), sl2, nm);
+          const float2 e2 = make_float2(ex2(x.x), ex2(x.y));
+          rs4[e] = __fadd2_rn(rs4[e], e2);
+          w[e] = pack2(e2.x, e2.y, BF16);
+        }
+        uint8_t* row = ptile + (gr >> 3) * (128 * 128) + r * 128;
+        *reinterpret_cast<uint4*>(row + (((gr & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      const float2 rs2 = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+      l = l * alpha + (rs2.x + rs2.y);
       tc::fence_async_shared();
       tc::tc_fence_before();
       tc::mbar_arrive(&p_full[g]);
@@ -349,6 +352,8 @@ __global__ void __launch_bounds__(320, 1)
         tc::tmem_ld32(tbase + C::T_O + c * 32 + lane_off, o0);
         if (nb1 > 0) tc::tmem_ld32(tbase + C::T_O + 128 + c * 32 + lane_off, o1);
         tc::tmem_wait_ld();
+        tc::reg_fence32(o0);
+        if (nb1 > 0) tc::reg_fence32(o1);
         if (qrow < p.Sq) {
           uint32_t w[16];
 #pragma unroll
@@ -439,9 +444,7 @@ int launch_fwd(const b2_attn_args* a, cudaStream_t st) {
   p.lse = a->lse;
   p.err = device_error_ptr();
   dim3 grid((unsigned)((a->Sq + 127) / 128), (unsigned)(a->B * a->H));
-  LaunchScope ls("attn_fwd_tc", st);
-  attn_fwd_tc<D, BF16><<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, p);
-  return after_launch("attn_fwd_tc");
+  return launch_pdl("attn_fwd_tc", attn_fwd_tc<D, BF16>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, p);
 }
 
 int attn_tc_fwd(const b2_attn_args* a, cudaStream_t st) {
@@ -527,6 +530,9 @@ __global__ void __launch_bounds__(320, 1)
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
+  // the previous kernel on the stream must be done before any global or tensor memory is touched;
+  // TMEM is allocated only after this wait, so a waiting CTA never holds columns another CTA needs
+  tc::pdl_wait();
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
     tc::tmem_relinquish();
@@ -535,6 +541,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  tc::pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -758,6 +765,8 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __rest
                                                      const float* __restrict__ lse, float2* __restrict__ lsed,
                                                      float* __restrict__ dq_acc, int64_t H, int64_t Sq, int64_t sq_pad,
                                                      int64_t o0, int64_t o1, int64_t o2, int64_t g0, int64_t g1, int64_t g2) {
+  tc::pdl_wait();
+  tc::pdl_trigger();
   const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
   const int64_t q0 = (int64_t)blockIdx.x * 64;
   // thread = (row, quarter of the 128-wide row): 4 x 16-byte loads of O and of dO, all in flight at once
@@ -800,6 +809,8 @@ __global__ void __launch_bounds__(256) attn_dq_convert(const float* __restrict__
                                                        int64_t H, int64_t Sq, int64_t sq_pad, int64_t s0, int64_t s1,
                                                        int64_t s2) {
   __shared__ float t[128][65];
+  tc::pdl_wait();
+  tc::pdl_trigger();
   const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
   const int64_t q0 = (int64_t)blockIdx.x * 64;
   const float4* src = reinterpret_cast<const float4*>(dq_acc + bh * 128 * sq_pad + q0);
@@ -862,11 +873,11 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   float2* lsed = reinterpret_cast<float2*>(dq_acc + a->B * a->H * a->D * sq_pad);
   {
     dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
-    LaunchScope ls("attn_bwd_prep", st);
-    attn_bwd_prep<<<grid, 256, 0, st>>>((const __nv_bfloat16*)a->o, (const __nv_bfloat16*)a->d_o, a->lse, lsed, dq_acc,
-                                        a->H, a->Sq, sq_pad, a->o_s[0], a->o_s[1], a->o_s[2], a->do_s[0], a->do_s[1],
-                                        a->do_s[2]);
-    if (int rc = after_launch("attn_bwd_prep")) return rc;
+    if (int rc = launch_pdl("attn_bwd_prep", attn_bwd_prep, grid, dim3(256), 0, st, (const __nv_bfloat16*)a->o,
+                            (const __nv_bfloat16*)a->d_o, (const float*)a->lse, lsed, dq_acc, (int64_t)a->H,
+                            (int64_t)a->Sq, sq_pad, a->o_s[0], a->o_s[1], a->o_s[2], a->do_s[0], a->do_s[1],
+                            a->do_s[2]))
+      return rc;
   }
   CUtensorMap tq, tk, tv, tdo;
   if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, 128, true, 64) ||
@@ -885,16 +896,16 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   p.err = device_error_ptr();
   {
     dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)(a->B * a->H));
-    LaunchScope ls("attn_bwd_tc", st);
-    attn_bwd_tc_kernel<<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, tdo, p, lsed, sq_pad);
-    if (int rc = after_launch("attn_bwd_tc")) return rc;
+    if (int rc = launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, tdo, p,
+                            (const float2*)lsed, sq_pad))
+      return rc;
   }
   if (a->dq) {
     dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
-    LaunchScope ls("attn_dq_convert", st);
-    attn_dq_convert<<<grid, 256, 0, st>>>(dq_acc, (__nv_bfloat16*)a->dq, a->H, a->Sq, sq_pad, a->dq_s[0], a->dq_s[1],
-                                          a->dq_s[2]);
-    if (int rc = after_launch("attn_dq_convert")) return rc;
+    if (int rc = launch_pdl("attn_dq_convert", attn_dq_convert, grid, dim3(256), 0, st, (const float*)dq_acc,
+                            (__nv_bfloat16*)a->dq, (int64_t)a->H, (int64_t)a->Sq, sq_pad, a->dq_s[0], a->dq_s[1],
+                            a->dq_s[2]))
+      return rc;
   }
   return 0;
 }

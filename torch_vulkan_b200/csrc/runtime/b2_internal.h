@@ -37,6 +37,43 @@ struct LaunchScope {
 // Checks cudaGetLastError after a launch.
 int after_launch(const char* what);
 
+// Programmatic dependent launch: a kernel launched this way may start (prologue: barrier init,
+// descriptor prefetch) while the previous kernel on the stream drains; it calls griddepcontrol.wait
+// before touching global memory or tensor memory. Eager launches only; off with B2_NO_PDL=1.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  // Under stream capture the plain edge is kept: replaying a graph whose kernel nodes carry
+  // programmatic edges measured slower on B200 than the same graph without them.
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (pdl_enabled() && cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cs = cudaStreamCaptureStatusActive;
+  }
+  cfg.numAttrs = (pdl_enabled() && cs == cudaStreamCaptureStatusNone) ? 1 : 0;
+  cudaError_t e;
+  {
+    LaunchScope ls(name, st);
+    e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+  }
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail_cuda(e, name);
+  }
+  return after_launch(name);
+}
+
 // Device error word (bounded waits that expired write a non-zero code here).
 int* device_error_ptr();
 void stat_add(int id, uint64_t v);

@@ -123,6 +123,14 @@ int ensure_init() {
   return 0;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B2_NO_PDL");
+    return !(e && *e && *e != '0');
+  }();
+  return on;
+}
+
 LaunchScope::LaunchScope(const char* kernel_name, cudaStream_t s) : name(kernel_name), stream(s) {
   g_stats[B2_STAT_LAUNCHES].fetch_add(1, std::memory_order_relaxed);
   if (profiling()) {
