@@ -14,7 +14,8 @@
 //           shared memory and dK, dV in TMEM while it walks 64-query tiles: S^T = K Q^T and
 //           dP^T = V dO^T on the tensor cores, P^T / dS^T in registers (thread = key row), then
 //           dV += P^T dO, dK += dS^T Q and dQ^T = K^T dS^T (all tcgen05); dQ partials are added into an
-//           fp32 workspace with vector atomics and converted at the end.
+//           fp32 workspace tile by tile with bulk reductions (cp.reduce.async.bulk, done in L2) and
+//           converted at the end.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code and unwinds.
 #include <cuda.h>
 
@@ -467,7 +468,7 @@ struct BwdCfg {
   static constexpr int QT_BYTES = BQ * D * 2;         // Q or dO tile, 16 KB
   static constexpr int PT_BYTES = BKV * BQ * 2;       // P^T or dS^T tile, 16 KB
   static constexpr int LD_BYTES = BQ * 8;             // (lse*log2e, delta) per query
-  static constexpr int QS = 3;                        // Q / dO / (lse, delta) prefetch depth
+  static constexpr int QS = 2;                        // Q / dO / (lse, delta) prefetch depth
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + KV_BYTES;
   static constexpr int OFF_Q = OFF_V + KV_BYTES;       // QS stages
@@ -475,7 +476,10 @@ struct BwdCfg {
   static constexpr int OFF_P = OFF_DO + QS * QT_BYTES;  // 2 buffers
   static constexpr int OFF_DS = OFF_P + 2 * PT_BYTES;   // 2 buffers
   static constexpr int OFF_LD = OFF_DS + 2 * PT_BYTES;  // QS stages
-  static constexpr int OFF_BAR = OFF_LD + QS * LD_BYTES;
+  // dQ^T tile staging (fp32): two 128-row x 32-float boxes in the 128-byte swizzled TMA layout
+  static constexpr int OFF_STG = (OFF_LD + QS * LD_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STG_BYTES = D * BQ * 4;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KB shared-memory limit");
   static constexpr int THREADS = 320;
@@ -486,7 +490,8 @@ struct BwdCfg {
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                       AttnTcParams p, const float2* __restrict__ lsed, int64_t sq_pad) {
+                       const __grid_constant__ CUtensorMap tmDQ, AttnTcParams p, const float2* __restrict__ lsed,
+                       int64_t sq_pad) {
   using C = BwdCfg;
   constexpr bool BF16 = true;
   extern __shared__ uint8_t smem_raw[];
@@ -505,6 +510,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* q_empty = bar + 10 + QS;  // [QS] all MMAs reading Q_i / dO_i done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10 + 2 * QS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 11 + 2 * QS);
+  uint64_t* stg_full = bar + 12 + 2 * QS;  // dQ^T staging tile written (count 256)
+  uint64_t* stg_free = bar + 13 + 2 * QS;  // the bulk reduction of the previous tile has read it
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = blockIdx.x * C::BKV;
@@ -527,6 +534,8 @@ __global__ void __launch_bounds__(320, 1)
     tc::mbar_init(dq_empty, 256);
     tc::mbar_init(dkv_full, 1);
     tc::mbar_init(sdp_empty, 256);
+    tc::mbar_init(stg_full, 256);
+    tc::mbar_init(stg_free, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -652,6 +661,12 @@ __global__ void __launch_bounds__(320, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
+    // dQ^T_i (fp32, [d][64 queries]) leaves TMEM through a shared-memory staging tile and is added to
+    // the accumulator tile [bh][i][d][64] by two TMA reductions performed in L2 (one per 32-query
+    // half), issued by thread ew == 0: no per-thread atomics. The scale is applied at conversion.
+    const int ew = threadIdx.x - 64;  // 0..255
+    uint8_t* stg = smem + C::OFF_STG;
+    const int64_t ntq = sq_pad / C::BQ;
     auto drain_dq = [&](int i) -> bool {
       if (!tc::mbar_wait(dq_full, (uint32_t)(i & 1), p.err)) return false;
       tc::tc_fence_after();
@@ -659,14 +674,30 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       tc::tmem_ld32(tbase + C::T_DQ + g * 32 + lane_off, v);
       tc::tmem_wait_ld();
+      tc::reg_fence32(v);
       tc::tc_fence_before();
       tc::mbar_arrive(dq_empty);
-      // dq_acc layout [bh][d][sq_pad]: thread d adds its 32 consecutive queries
-      float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((int64_t)bh * C::D + r) * sq_pad + (int64_t)i * C::BQ + g * 32);
+      if (i > 0) {
+        if (ew == 0) {
+          tc::bulk_wait_read0();
+          tc::mbar_arrive(stg_free);
+        }
+        if (!tc::mbar_wait(stg_free, (uint32_t)((i - 1) & 1), p.err)) return false;
+      }
+      // box g, row d = r: 8 16-byte chunks at their 128-byte-swizzle positions (conflict-free)
+      uint8_t* row = stg + g * (C::D * 128) + r * 128;
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        atomicAdd(dst + e, make_float4(__uint_as_float(v[4 * e]) * p.scale, __uint_as_float(v[4 * e + 1]) * p.scale,
-                                       __uint_as_float(v[4 * e + 2]) * p.scale, __uint_as_float(v[4 * e + 3]) * p.scale));
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      tc::fence_async_shared();
+      tc::mbar_arrive(stg_full);
+      if (ew == 0) {
+        if (!tc::mbar_wait(stg_full, (uint32_t)(i & 1), p.err)) return false;
+        const int32_t y = (int32_t)(((int64_t)bh * ntq + i) * C::D);
+        tc::tma_reduce_add_2d(&tmDQ, stg, 0, y);
+        tc::tma_reduce_add_2d(&tmDQ, stg + C::D * 128, 32, y);
+        tc::bulk_commit();
+      }
       return true;
     };
     for (int i = 0; i < ntile; ++i) {
@@ -717,6 +748,7 @@ __global__ void __launch_bounds__(320, 1)
       if (i > 0 && !drain_dq(i - 1)) { ok = false; break; }
     }
     if (ok && ntile > 0) ok = drain_dq(ntile - 1);
+    if (ew == 0) tc::bulk_wait0();
     // ---------------- dK, dV epilogue: group g writes d columns [64g, 64g+64) ----------------
     if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
       tc::tc_fence_after();
@@ -760,7 +792,7 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // Pre-pass, one block per (64-query tile, batch*head): lsed[bh][q] = (lse*log2e, rowsum(O*dO)) with
-// (+inf, 0) for padding rows, and zero the tile's slice of the fp32 dQ accumulator [bh][d][sq_pad].
+// (+inf, 0) for padding rows, and zero the tile of the fp32 dQ accumulator [bh][q/64][d][64].
 __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                                      const float* __restrict__ lse, float2* __restrict__ lsed,
                                                      float* __restrict__ dq_acc, int64_t H, int64_t Sq, int64_t sq_pad,
@@ -794,33 +826,28 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __rest
   s += __shfl_xor_sync(0xffffffffu, s, 2);
   if (qtr == 0)
     lsed[bh * sq_pad + q] = q < Sq ? make_float2(lse[bh * Sq + q] * 1.4426950408889634f, s) : make_float2(INFINITY, 0.f);
-  float4* acc = reinterpret_cast<float4*>(dq_acc + bh * 128 * sq_pad + q0);
-  const int64_t row4 = sq_pad / 4;
+  float4* acc = reinterpret_cast<float4*>(dq_acc + (bh * (sq_pad / 64) + blockIdx.x) * (128 * 64));
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int e = threadIdx.x + it * 256;  // 128 d-rows x 16 float4
-    acc[(e >> 4) * row4 + (e & 15)] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int it = 0; it < 8; ++it) acc[threadIdx.x + it * 256] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dq[b,h,q,:] = bf16(dq_acc[bh][:][q]), one block per (64-query tile, batch*head), transposed through
 // shared memory so both the fp32 reads and the bf16 writes are 16-byte and coalesced.
 __global__ void __launch_bounds__(256) attn_dq_convert(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dq,
                                                        int64_t H, int64_t Sq, int64_t sq_pad, int64_t s0, int64_t s1,
-                                                       int64_t s2) {
+                                                       int64_t s2, float scale) {
   __shared__ float t[128][65];
   tc::pdl_wait();
   tc::pdl_trigger();
   const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
   const int64_t q0 = (int64_t)blockIdx.x * 64;
-  const float4* src = reinterpret_cast<const float4*>(dq_acc + bh * 128 * sq_pad + q0);
-  const int64_t row4 = sq_pad / 4;
+  const float4* src = reinterpret_cast<const float4*>(dq_acc + (bh * (sq_pad / 64) + blockIdx.x) * (128 * 64));
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int e = threadIdx.x + it * 256;
     const int d = e >> 4, j = (e & 15) * 4;
-    float4 v = src[d * row4 + (e & 15)];
-    t[d][j] = v.x, t[d][j + 1] = v.y, t[d][j + 2] = v.z, t[d][j + 3] = v.w;
+    float4 v = src[e];
+    t[d][j] = v.x * scale, t[d][j + 1] = v.y * scale, t[d][j + 2] = v.z * scale, t[d][j + 3] = v.w * scale;
   }
   __syncthreads();
 #pragma unroll
@@ -841,6 +868,7 @@ __global__ void __launch_bounds__(256) attn_dq_convert(const float* __restrict__
 bool attn_tc_bwd_eligible(const b2_attn_args* a) {
   if (!attn_tc_eligible(a) || a->D != 128 || a->dtype != B2_BF16) return false;
   if (!strides_ok(a->do_s, a->B, a->H, a->Sq) || ((uintptr_t)a->d_o & 15)) return false;
+  if (a->B * a->H * ((a->Sq + 63) / 64 * 64) * 2 >= (1ll << 31)) return false;  // dQ accumulator rows fit int32
   if ((a->do_s[2] % 8) || (a->do_s[1] % 8) || (a->do_s[0] % 8)) return false;
   auto al = [](const void* p) { return p == nullptr || ((uintptr_t)p & 15) == 0; };
   if (!al(a->dk) || !al(a->dv) || !al(a->dq)) return false;
@@ -849,7 +877,7 @@ bool attn_tc_bwd_eligible(const b2_attn_args* a) {
   return true;
 }
 
-// workspace = fp32 dQ accumulator [B*H][D][sq_pad] followed by (lse*log2e, delta) [B*H][sq_pad]
+// workspace = fp32 dQ accumulator [B*H][sq_pad/64][D][64] followed by (lse*log2e, delta) [B*H][sq_pad]
 uint64_t attn_bwd_ws_bytes(const b2_attn_args* a) {
   if (!attn_tc_bwd_eligible(a)) return 0;
   const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
@@ -879,7 +907,15 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
                             a->do_s[2]))
       return rc;
   }
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
+  {
+    // dQ accumulator as [B*H*sq_pad/64*D rows][64 fp32], reduced into in 128 x 32 boxes
+    const uint64_t dims[2] = {64, (uint64_t)(a->B * a->H * (sq_pad / 64) * 128)};
+    const uint64_t strides[1] = {256};
+    const uint32_t box[2] = {32, 128};
+    if (!make_tmap(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(B2_ERR_ARG, "attn_bwd_tc: dQ accumulator tensor map rejected");
+  }
   if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, 128, true, 64) ||
       !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, 128, true, 128) ||
       !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, 128, true, 128) ||
@@ -896,7 +932,7 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   p.err = device_error_ptr();
   {
     dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)(a->B * a->H));
-    if (int rc = launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, tdo, p,
+    if (int rc = launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, tdo, tdq, p,
                             (const float2*)lsed, sq_pad))
       return rc;
   }
@@ -904,7 +940,7 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
     dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
     if (int rc = launch_pdl("attn_dq_convert", attn_dq_convert, grid, dim3(256), 0, st, (const float*)dq_acc,
                             (__nv_bfloat16*)a->dq, (int64_t)a->H, (int64_t)a->Sq, sq_pad, a->dq_s[0], a->dq_s[1],
-                            a->dq_s[2]))
+                            a->dq_s[2], a->scale))
       return rc;
   }
   return 0;
