@@ -73,16 +73,16 @@ struct FwdCfg {
   static constexpr int Q_BYTES = BQ * D * 2;
   static constexpr int K_BYTES = BKV * D * 2;
   static constexpr int V_BYTES = BKV * D * 2;
-  static constexpr int P_BYTES = BQ * BKV * 2;
-  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_Q = 0;                    // also the (m, l) exchange area of the epilogue
   static constexpr int OFF_K = OFF_Q + Q_BYTES;      // 2 stages
   static constexpr int OFF_V = OFF_K + 2 * K_BYTES;  // 2 stages
-  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;  // P[0] even blocks, P[1] odd blocks
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_BAR = OFF_V + 2 * V_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "forward tile set exceeds the 227 KB shared-memory limit");
+  static_assert(Q_BYTES >= 2 * BQ * 8, "exchange area");
   static constexpr int THREADS = 320;
-  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D)
+  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D); P_g (bf16 pairs) overwrites
+  // the first 64 columns of S_g once the softmax has read S_g into registers
   static constexpr uint32_t T_S = 0, T_O = 256, TMEM_COLS = 512;
 };
 
@@ -100,11 +100,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* v_full = bar + 5;   // [2]
   uint64_t* v_empty = bar + 7;  // [2]
   uint64_t* s_full = bar + 9;   // [2] S of block j into S[j&1]
-  uint64_t* p_full = bar + 11;  // [2] P of block j into P[j&1] (count 128)
+  uint64_t* p_full = bar + 11;  // [2] P of block j into TMEM over S[j&1] (count 128)
   uint64_t* o_upd = bar + 13;   // [2] PV of block j into O[j&1] done
-  uint64_t* s_free = bar + 15;  // [2] S[j&1] of block j read into registers (count 128)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 18);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * C::BQ;
@@ -122,7 +121,6 @@ __global__ void __launch_bounds__(320, 1)
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 128);
       tc::mbar_init(&o_upd[i], 1);
-      tc::mbar_init(&s_free[i], 128);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -142,32 +140,25 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: Q, K_0, K_1, then V_j followed by K_j+2 ----------------
-      // (the order in which the MMA warp consumes them: S_j+2 is issued before PV_j)
+      // ---------------- producer: Q once, then K_j / V_j into 2-stage rings ----------------
       bool ok = true;
       tc::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
       for (int c = 0; c < C::DCH; ++c) tc::tma_load_4d(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, q_full, c * 64, q0, h, b);
       int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};
-      auto load_k = [&](int j) -> bool {
+      for (int j = 0; j < nblk && ok; ++j) {
         const int s = j & 1;
-        if (!tc::mbar_wait(&k_empty[s], (uint32_t)(((j >> 1) & 1) ^ 1), p.err) || *abort_flag) return false;
+        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        if (!tc::mbar_wait(&k_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
         tc::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
         for (int c = 0; c < C::DCH; ++c)
           tc::tma_load_4d(smem + C::OFF_K + s * C::K_BYTES + c * (C::BKV * 128), &tmK, &k_full[s], c * 64, j * C::BKV, h, b);
         issued_k[s]++;
-        return true;
-      };
-      auto load_v = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!tc::mbar_wait(&v_empty[s], (uint32_t)(((j >> 1) & 1) ^ 1), p.err) || *abort_flag) return false;
+        if (!tc::mbar_wait(&v_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
         tc::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
         for (int c = 0; c < C::DCH; ++c)
           tc::tma_load_4d(smem + C::OFF_V + s * C::V_BYTES + c * (C::BKV * 128), &tmV, &v_full[s], c * 64, j * C::BKV, h, b);
         issued_v[s]++;
-        return true;
-      };
-      ok = load_k(0) && (nblk < 2 || load_k(1));
-      for (int j = 0; j < nblk && ok; ++j) ok = load_v(j) && (j + 2 >= nblk || load_k(j + 2));
+      }
       if (!ok) {
         *abort_flag = 1;
         tc::mbar_wait(q_full, 0, nullptr);
@@ -180,9 +171,9 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      // For block j: S_j+2 (into the TMEM tile of S_j) as soon as the softmax group has read S_j into
-      // registers, then PV_j once its P tile is in shared memory. S_j+2 thus runs on the tensor cores
-      // while the softmax of S_j is still being computed.
+      // S_j = Q K_j^T into S[j&1]; once the softmax has replaced S_j by P_j (bf16, in TMEM),
+      // O[j&1] += P_j V_j with A read from TMEM, then S_j+2 into the same columns: tcgen05.mma from
+      // one thread executes in order, so S_j+2 cannot overwrite P_j before PV_j has read it.
       constexpr uint32_t IDESC_S = tc::idesc_f16(128, C::BKV, BF16, false, false);  // Q K^T: both K-major
       constexpr uint32_t IDESC_O = tc::idesc_f16(128, D, BF16, false, true);        // P V: V is MN-major
       const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q);
@@ -206,27 +197,22 @@ __global__ void __launch_bounds__(320, 1)
       if (ok && nblk > 1) ok = issue_s(1);
       for (int j = 0; j < nblk && ok; ++j) {
         const int s = j & 1;
-        if (j + 2 < nblk) {
-          if (!tc::mbar_wait(&s_free[s], (uint32_t)((j >> 1) & 1), p.err)) { ok = false; break; }
-          tc::tc_fence_after();
-          if (!issue_s(j + 2)) { ok = false; break; }
-        }
         if (!tc::mbar_wait(&p_full[s], (uint32_t)((j >> 1) & 1), p.err) ||
             !tc::mbar_wait(&v_full[s], (uint32_t)((j >> 1) & 1), p.err)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        const uint32_t p_addr = tc::smem_u32(smem + C::OFF_P + s * C::P_BYTES);
         const uint32_t v_addr = tc::smem_u32(smem + C::OFF_V + s * C::V_BYTES);
 #pragma unroll
         for (int k = 0; k < C::BKV / 16; ++k) {
-          const uint64_t ad = tc::sdesc_sw128(p_addr + (k >> 2) * (128 * 128) + (k & 3) * 32, 16, 1024);
           const uint64_t bd = tc::sdesc_sw128(v_addr + k * 2048, C::BKV * 128, 1024);
-          tc::mma_f16_ss(tbase + C::T_O + s * 128, ad, bd, IDESC_O, (j >= 2 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tbase + C::T_O + s * 128, tbase + C::T_S + s * 128 + k * 8, bd, IDESC_O,
+                         (j >= 2 || k > 0) ? 1u : 0u);
         }
         tc::mma_commit(&o_upd[s]);
         tc::mma_commit(&v_empty[s]);
+        if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
       }
       if (!ok) *abort_flag = 1;
     }
@@ -242,12 +228,12 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     int kb = 0;  // blocks processed by this warpgroup
     for (int j = g; j < nblk; j += 2, ++kb) {
+      // S_j complete implies PV_j-2 of this group complete (issued before it, in-order execution)
       if (!tc::mbar_wait(&s_full[g], (uint32_t)(kb & 1), p.err) || *abort_flag) {
         ok = false;
         break;
       }
       tc::tc_fence_after();
-      // the whole 128-column S row in registers; TMEM S goes back to the next S MMA right away
       uint32_t sr[128];
       __syncwarp();
 #pragma unroll
@@ -255,8 +241,6 @@ __global__ void __launch_bounds__(320, 1)
       tc::tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 4; ++c) tc::reg_fence32(sr + 32 * c);
-      tc::tc_fence_before();
-      tc::mbar_arrive(&s_free[g]);
       const int64_t rem = p.Sk - (int64_t)j * C::BKV;
       if (rem < C::BKV) {  // ragged last block: keys past the end contribute exp2(-inf) = 0
 #pragma unroll
@@ -279,59 +263,49 @@ __global__ void __launch_bounds__(320, 1)
         alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
         m = m_new;
       }
-      // PV of this group's previous block must be complete before its P tile is overwritten and
-      // before O is rescaled (it was issued when that P tile was published, so the wait is short)
-      if (kb > 0) {
-        if (!tc::mbar_wait(&o_upd[g], (uint32_t)((kb - 1) & 1), p.err)) {
-          ok = false;
-          break;
-        }
-        tc::tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
+      if (kb > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the S row is still in registers
-            uint32_t orow[16];
-            tc::tmem_ld16(t_o + c * 16 + lane_off, orow);
-            tc::tmem_wait_ld();
-            tc::reg_fence16(orow);
+        for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the S row is still in registers
+          uint32_t orow[16];
+          tc::tmem_ld16(t_o + c * 16 + lane_off, orow);
+          tc::tmem_wait_ld();
+          tc::reg_fence16(orow);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
-            tc::tmem_st16(t_o + c * 16 + lane_off, orow);
-          }
-          tc::tmem_wait_st();
+          for (int e = 0; e < 16; ++e) orow[e] = __float_as_uint(__uint_as_float(orow[e]) * alpha);
+          tc::tmem_st16(t_o + c * 16 + lane_off, orow);
         }
       }
-      // P = exp2(s * scale_log2 - m) as 16-bit pairs, 8 keys (one 16-byte granule) at a time into the
-      // 128-byte swizzled K-major A tile of the PV MMA
+      // P = exp2(s * scale_log2 - m) as 16-bit pairs, 64 keys at a time into TMEM columns [0, 64)
+      // of this group's S tile: the A operand of the PV MMA
       const float2 nm = make_float2(-m, -m);
       float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      uint8_t* ptile = smem + C::OFF_P + g * C::P_BYTES;
 #pragma unroll
-      for (int gr = 0; gr < 16; ++gr) {
-        uint32_t w[4];
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t w[32];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = gr * 8 + 2 * e;
-          const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])), sl2, nm);
+        for (int i = 0; i < 32; ++i) {
+          const int c = hh * 64 + 2 * i;
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sl2, nm);
           const float2 e2 = make_float2(ex2(x.x), ex2(x.y));
-          rs4[e] = __fadd2_rn(rs4[e], e2);
-          w[e] = pack2(e2.x, e2.y, BF16);
+          rs4[i & 3] = __fadd2_rn(rs4[i & 3], e2);
+          w[i] = pack2(e2.x, e2.y, BF16);
         }
-        uint8_t* row = ptile + (gr >> 3) * (128 * 128) + r * 128;
-        *reinterpret_cast<uint4*>(row + (((gr & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tc::tmem_st32(t_s + hh * 32 + lane_off, w);
       }
       const float2 rs2 = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
       l = l * alpha + (rs2.x + rs2.y);
-      tc::fence_async_shared();
+      tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(&p_full[g]);
     }
     // ---------------- epilogue: combine the two groups, O / l -> global, lse ----------------
+    // Each group's last PV completing implies every S MMA (hence every read of Q) is done, so the
+    // (m, l) exchange can use the Q tile.
     const int nb0 = (nblk + 1) / 2, nb1 = nblk / 2;
     if (ok && kb > 0 && !tc::mbar_wait(&o_upd[g], (uint32_t)((kb - 1) & 1), p.err)) ok = false;
-    // (m, l) exchange through the start of each group's own P buffer: its last PV has completed
-    float2* x0p = reinterpret_cast<float2*>(smem + C::OFF_P);
-    float2* x1p = reinterpret_cast<float2*>(smem + C::OFF_P + C::P_BYTES);
+    float2* x0p = reinterpret_cast<float2*>(smem + C::OFF_Q);
+    float2* x1p = x0p + C::BQ;
+    tc::named_bar_sync(1, 256);  // both groups past their last PV before the Q tile is overwritten
     (g ? x1p : x0p)[r] = make_float2(m, l);
     tc::named_bar_sync(1, 256);
     if (ok && !*abort_flag) {
