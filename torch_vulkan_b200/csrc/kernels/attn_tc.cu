@@ -73,10 +73,11 @@ struct FwdCfg {
   static constexpr int Q_BYTES = BQ * D * 2;
   static constexpr int K_BYTES = BKV * D * 2;
   static constexpr int V_BYTES = BKV * D * 2;
-  static constexpr int OFF_Q = 0;                    // also the (m, l) exchange area of the epilogue
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;      // 2 stages
-  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;  // 2 stages
-  static constexpr int OFF_BAR = OFF_V + 2 * V_BYTES;
+  static constexpr int NS = 3;                        // K / V ring depth
+  static constexpr int OFF_Q = 0;                     // also the (m, l) exchange area of the epilogue
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;       // NS stages
+  static constexpr int OFF_V = OFF_K + NS * K_BYTES;  // NS stages
+  static constexpr int OFF_BAR = OFF_V + NS * V_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(SMEM <= 232448, "forward tile set exceeds the 227 KB shared-memory limit");
   static_assert(Q_BYTES >= 2 * BQ * 8, "exchange area");
@@ -94,16 +95,17 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  constexpr int NS = C::NS;
   uint64_t* q_full = bar + 0;
-  uint64_t* k_full = bar + 1;   // [2]
-  uint64_t* k_empty = bar + 3;  // [2]
-  uint64_t* v_full = bar + 5;   // [2]
-  uint64_t* v_empty = bar + 7;  // [2]
-  uint64_t* s_full = bar + 9;   // [2] S of block j into S[j&1]
-  uint64_t* p_full = bar + 11;  // [2] P of block j into TMEM over S[j&1] (count 128)
-  uint64_t* o_upd = bar + 13;   // [2] PV of block j into O[j&1] done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 15);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 16);
+  uint64_t* k_full = bar + 1;             // [NS] K of block j in stage j % NS
+  uint64_t* k_empty = k_full + NS;        // [NS]
+  uint64_t* v_full = k_empty + NS;        // [NS]
+  uint64_t* v_empty = v_full + NS;        // [NS]
+  uint64_t* s_full = v_empty + NS;        // [2] S of block j into S[j&1]
+  uint64_t* p_full = s_full + 2;          // [2] P of block j into TMEM over S[j&1] (count 128)
+  uint64_t* o_upd = p_full + 2;           // [2] PV of block j into O[j&1] done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_upd + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(o_upd + 3);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * C::BQ;
@@ -113,11 +115,13 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       tc::mbar_init(&k_full[i], 1);
       tc::mbar_init(&k_empty[i], 1);
       tc::mbar_init(&v_full[i], 1);
       tc::mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s_full[i], 1);
       tc::mbar_init(&p_full[i], 128);
       tc::mbar_init(&o_upd[i], 1);
@@ -140,14 +144,14 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- producer: Q once, then K_j / V_j into 2-stage rings ----------------
+      // ---------------- producer: Q once, then K_j / V_j into NS-stage rings ----------------
       bool ok = true;
       tc::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
       for (int c = 0; c < C::DCH; ++c) tc::tma_load_4d(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, q_full, c * 64, q0, h, b);
-      int issued_k[2] = {0, 0}, issued_v[2] = {0, 0};
+      int issued_k[NS] = {}, issued_v[NS] = {};
       for (int j = 0; j < nblk && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        const int s = j % NS;
+        const uint32_t ph = (uint32_t)((j / NS) & 1);
         if (!tc::mbar_wait(&k_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
         tc::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
         for (int c = 0; c < C::DCH; ++c)
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(320, 1)
       if (!ok) {
         *abort_flag = 1;
         tc::mbar_wait(q_full, 0, nullptr);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < NS; ++s) {
           if (issued_k[s]) tc::mbar_wait(&k_full[s], (uint32_t)((issued_k[s] - 1) & 1), nullptr);
           if (issued_v[s]) tc::mbar_wait(&v_full[s], (uint32_t)((issued_v[s] - 1) & 1), nullptr);
         }
@@ -179,10 +183,10 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q);
       bool ok = tc::mbar_wait(q_full, 0, p.err);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!tc::mbar_wait(&k_full[s], (uint32_t)((j >> 1) & 1), p.err)) return false;
+        const int s = j & 1, ks = j % NS;
+        if (!tc::mbar_wait(&k_full[ks], (uint32_t)((j / NS) & 1), p.err)) return false;
         tc::tc_fence_after();
-        const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K + s * C::K_BYTES);
+        const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K + ks * C::K_BYTES);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (k >> 2) * (128 * 128) + (k & 3) * 32;
@@ -190,20 +194,20 @@ __global__ void __launch_bounds__(320, 1)
                          tc::sdesc_sw128(k_addr + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
         }
         tc::mma_commit(&s_full[s]);
-        tc::mma_commit(&k_empty[s]);
+        tc::mma_commit(&k_empty[ks]);
         return true;
       };
       if (ok) ok = issue_s(0);
       if (ok && nblk > 1) ok = issue_s(1);
       for (int j = 0; j < nblk && ok; ++j) {
-        const int s = j & 1;
+        const int s = j & 1, ks = j % NS;
         if (!tc::mbar_wait(&p_full[s], (uint32_t)((j >> 1) & 1), p.err) ||
-            !tc::mbar_wait(&v_full[s], (uint32_t)((j >> 1) & 1), p.err)) {
+            !tc::mbar_wait(&v_full[ks], (uint32_t)((j / NS) & 1), p.err)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        const uint32_t v_addr = tc::smem_u32(smem + C::OFF_V + s * C::V_BYTES);
+        const uint32_t v_addr = tc::smem_u32(smem + C::OFF_V + ks * C::V_BYTES);
 #pragma unroll
         for (int k = 0; k < C::BKV / 16; ++k) {
           const uint64_t bd = tc::sdesc_sw128(v_addr + k * 2048, C::BKV * 128, 1024);
@@ -211,7 +215,7 @@ __global__ void __launch_bounds__(320, 1)
                          (j >= 2 || k > 0) ? 1u : 0u);
         }
         tc::mma_commit(&o_upd[s]);
-        tc::mma_commit(&v_empty[s]);
+        tc::mma_commit(&v_empty[ks]);
         if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
       }
       if (!ok) *abort_flag = 1;
@@ -442,23 +446,24 @@ struct BwdCfg {
   static constexpr int QT_BYTES = BQ * D * 2;         // Q or dO tile, 16 KB
   static constexpr int PT_BYTES = BKV * BQ * 2;       // P^T or dS^T tile, 16 KB
   static constexpr int LD_BYTES = BQ * 8;             // (lse*log2e, delta) per query
-  static constexpr int QS = 2;                        // Q / dO / (lse, delta) prefetch depth
+  static constexpr int QS = 3;                        // Q / dO / (lse, delta) prefetch depth
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + KV_BYTES;
   static constexpr int OFF_Q = OFF_V + KV_BYTES;       // QS stages
   static constexpr int OFF_DO = OFF_Q + QS * QT_BYTES;  // QS stages
-  static constexpr int OFF_P = OFF_DO + QS * QT_BYTES;  // 2 buffers
-  static constexpr int OFF_DS = OFF_P + 2 * PT_BYTES;   // 2 buffers
+  static constexpr int OFF_DS = OFF_DO + QS * QT_BYTES;  // dS^T, 2 buffers (B operand of dQ^T)
   static constexpr int OFF_LD = OFF_DS + 2 * PT_BYTES;  // QS stages
   // dQ^T tile staging (fp32): two 128-row x 32-float boxes in the 128-byte swizzled TMA layout
-  static constexpr int OFF_STG = (OFF_LD + QS * LD_BYTES + 1023) / 1024 * 1024;
+  static constexpr int OFF_BAR = OFF_LD + QS * LD_BYTES;  // 256 bytes in the alignment gap before the staging tile
+  static constexpr int OFF_STG = (OFF_BAR + 256 + 1023) / 1024 * 1024;
   static constexpr int STG_BYTES = D * BQ * 4;
-  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int SMEM = OFF_STG + STG_BYTES + 1024;
   static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KB shared-memory limit");
   static constexpr int THREADS = 320;
-  // TMEM columns: S^T [0,64) dP^T [64,128) dQ^T [128,192) dV [256,384) dK [384,512)
-  static constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_DV = 256, T_DK = 384, TMEM_COLS = 512;
+  // TMEM columns: S^T [0,64) dP^T [64,128) dQ^T [128,192) P^T [192,224) dS^T [224,256) (bf16 pairs,
+  // A operands of dV / dK) dV [256,384) dK [384,512)
+  static constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_PT = 192, T_DST = 224, T_DV = 256, T_DK = 384,
+                            TMEM_COLS = 512;
 };
 
 __global__ void __launch_bounds__(320, 1)
@@ -486,6 +491,7 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + 11 + 2 * QS);
   uint64_t* stg_full = bar + 12 + 2 * QS;  // dQ^T staging tile written (count 256)
   uint64_t* stg_free = bar + 13 + 2 * QS;  // the bulk reduction of the previous tile has read it
+  uint64_t* ptm_empty = bar + 14 + 2 * QS;  // dV / dK MMAs of the previous tile read P^T / dS^T in TMEM
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = blockIdx.x * C::BKV;
@@ -510,6 +516,7 @@ __global__ void __launch_bounds__(320, 1)
     tc::mbar_init(sdp_empty, 256);
     tc::mbar_init(stg_full, 256);
     tc::mbar_init(stg_free, 1);
+    tc::mbar_init(ptm_empty, 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -602,18 +609,18 @@ __global__ void __launch_bounds__(320, 1)
         tc::tc_fence_after();
         const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + qs * C::QT_BYTES);
         const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + qs * C::QT_BYTES);
-        const uint32_t pt_addr = tc::smem_u32(smem + C::OFF_P + s * C::PT_BYTES);
         const uint32_t ds_addr = tc::smem_u32(smem + C::OFF_DS + s * C::PT_BYTES);
-        // dV += P^T dO ; dK += dS^T Q   (M = 128 keys, N = D, K = 64 queries)
+        // dV += P^T dO ; dK += dS^T Q   (M = 128 keys, N = D, K = 64 queries; A from TMEM)
 #pragma unroll
         for (int k = 0; k < C::BQ / 16; ++k)
-          tc::mma_f16_ss(tbase + C::T_DV, tc::sdesc_sw128(pt_addr + k * 32, 16, 1024),
-                         tc::sdesc_sw128(do_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tbase + C::T_DV, tbase + C::T_PT + k * 8, tc::sdesc_sw128(do_addr + k * 2048, C::BQ * 128, 1024),
+                         IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
         for (int k = 0; k < C::BQ / 16; ++k)
-          tc::mma_f16_ss(tbase + C::T_DK, tc::sdesc_sw128(ds_addr + k * 32, 16, 1024),
-                         tc::sdesc_sw128(q_addr + k * 2048, C::BQ * 128, 1024), IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tbase + C::T_DK, tbase + C::T_DST + k * 8, tc::sdesc_sw128(q_addr + k * 2048, C::BQ * 128, 1024),
+                         IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
         tc::mma_commit(&q_empty[qs]);
+        tc::mma_commit(ptm_empty);
         // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
         if (i > 0 && !tc::mbar_wait(dq_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
         tc::tc_fence_after();
@@ -689,33 +696,37 @@ __global__ void __launch_bounds__(320, 1)
       tc::tmem_wait_ld();
       tc::tc_fence_before();
       tc::mbar_arrive(sdp_empty);
-      // P^T / dS^T buffer s was last read by the MMAs of tile i-2
-      if (i >= 2 && !tc::mbar_wait(&pds_empty[s], (uint32_t)(((i - 2) >> 1) & 1), p.err)) { ok = false; break; }
       const float2* ld = reinterpret_cast<const float2*>(smem + C::OFF_LD + qs * C::LD_BYTES) + g * 32;
-      uint8_t* pt = smem + C::OFF_P + s * C::PT_BYTES + r * 128;
+      uint32_t wp[16], wd[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        float pv[2], dv[2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int c = 2 * e + t;
+          const float2 L = ld[c];  // (lse * log2e, delta); padding rows hold (+inf, 0)
+          const float pp = ex2(__uint_as_float(sv[c]) * p.scale_log2 - L.x);
+          pv[t] = pp;
+          dv[t] = pp * (__uint_as_float(dp[c]) - L.y);
+        }
+        wp[e] = pack2(pv[0], pv[1], BF16);
+        wd[e] = pack2(dv[0], dv[1], BF16);
+      }
+      // P^T / dS^T in TMEM were read by the dV / dK MMAs of tile i-1
+      if (i >= 1 && !tc::mbar_wait(ptm_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
+      tc::tc_fence_after();
+      tc::tmem_st16(tbase + C::T_PT + g * 16 + lane_off, wp);
+      tc::tmem_st16(tbase + C::T_DST + g * 16 + lane_off, wd);
+      // dS^T buffer s in shared memory was last read by the dQ^T MMA of tile i-2
+      if (i >= 2 && !tc::mbar_wait(&pds_empty[s], (uint32_t)(((i - 2) >> 1) & 1), p.err)) { ok = false; break; }
       uint8_t* dst = smem + C::OFF_DS + s * C::PT_BYTES + r * 128;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 queries
-        uint32_t wp[4], wd[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int c = q4 * 8 + 2 * e + t;
-            const float2 L = ld[c];  // (lse * log2e, delta); padding rows hold (+inf, 0)
-            const float pp = ex2(__uint_as_float(sv[c]) * p.scale_log2 - L.x);
-            pv[t] = pp;
-            dv[t] = pp * (__uint_as_float(dp[c]) - L.y);
-          }
-          wp[e] = pack2(pv[0], pv[1], BF16);
-          wd[e] = pack2(dv[0], dv[1], BF16);
-        }
+      for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 queries, 128-byte swizzled rows
         const int gr = g * 4 + q4;
-        const int off = ((gr ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(pt + off) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
-        *reinterpret_cast<uint4*>(dst + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        *reinterpret_cast<uint4*>(dst + ((gr ^ (r & 7)) << 4)) =
+            make_uint4(wd[4 * q4], wd[4 * q4 + 1], wd[4 * q4 + 2], wd[4 * q4 + 3]);
       }
+      tc::tmem_wait_st();
       tc::fence_async_shared();
       tc::tc_fence_before();
       tc::mbar_arrive(&pds_full[s]);
