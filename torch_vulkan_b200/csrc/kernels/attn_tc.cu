@@ -180,18 +180,18 @@ __global__ void __launch_bounds__(320, 1)
       // one thread executes in order, so S_j+2 cannot overwrite P_j before PV_j has read it.
       constexpr uint32_t IDESC_S = tc::idesc_f16(128, C::BKV, BF16, false, false);  // Q K^T: both K-major
       constexpr uint32_t IDESC_O = tc::idesc_f16(128, D, BF16, false, true);        // P V: V is MN-major
-      const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q);
+      const tc::SDesc qd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_Q), 16, 1024);
       bool ok = tc::mbar_wait(q_full, 0, p.err);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1, ks = j % NS;
         if (!tc::mbar_wait(&k_full[ks], (uint32_t)((j / NS) & 1), p.err)) return false;
         tc::tc_fence_after();
-        const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K + ks * C::K_BYTES);
+        const tc::SDesc kd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_K + ks * C::K_BYTES), 16, 1024);
+        const uint32_t dst = tbase + C::T_S + s * 128;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (k >> 2) * (128 * 128) + (k & 3) * 32;
-          tc::mma_f16_ss(tbase + C::T_S + s * 128, tc::sdesc_sw128(q_addr + off, 16, 1024),
-                         tc::sdesc_sw128(k_addr + off, 16, 1024), IDESC_S, k > 0 ? 1u : 0u);
+          tc::mma_f16_ss(dst, tc::sdesc_at(qd, off), tc::sdesc_at(kd, off), IDESC_S, k > 0 ? 1u : 0u);
         }
         tc::mma_commit(&s_full[s]);
         tc::mma_commit(&k_empty[ks]);
@@ -207,13 +207,12 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc::tc_fence_after();
-        const uint32_t v_addr = tc::smem_u32(smem + C::OFF_V + ks * C::V_BYTES);
+        const tc::SDesc vd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_V + ks * C::V_BYTES), C::BKV * 128, 1024);
+        const uint32_t o_dst = tbase + C::T_O + s * 128, p_src = tbase + C::T_S + s * 128;
+        const uint32_t acc0 = j >= 2 ? 1u : 0u;
 #pragma unroll
-        for (int k = 0; k < C::BKV / 16; ++k) {
-          const uint64_t bd = tc::sdesc_sw128(v_addr + k * 2048, C::BKV * 128, 1024);
-          tc::mma_f16_ts(tbase + C::T_O + s * 128, tbase + C::T_S + s * 128 + k * 8, bd, IDESC_O,
-                         (j >= 2 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < C::BKV / 16; ++k)
+          tc::mma_f16_ts(o_dst, p_src + k * 8, tc::sdesc_at(vd, k * 2048), IDESC_O, k > 0 ? 1u : acc0);
         tc::mma_commit(&o_upd[s]);
         tc::mma_commit(&v_empty[ks]);
         if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
@@ -459,14 +458,17 @@ struct BwdCfg {
   static constexpr int STG_BYTES = D * BQ * 4;
   static constexpr int SMEM = OFF_STG + STG_BYTES + 1024;
   static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KB shared-memory limit");
-  static constexpr int THREADS = 320;
+  static constexpr int NG = 4;                 // element-wise warpgroups, each owning BQ / NG query columns
+  static constexpr int QPG = BQ / NG;          // 16
+  static constexpr int NEW = 128 * NG;         // element-wise threads
+  static constexpr int THREADS = 64 + NEW;
   // TMEM columns: S^T [0,64) dP^T [64,128) dQ^T [128,192) P^T [192,224) dS^T [224,256) (bf16 pairs,
   // A operands of dV / dK) dV [256,384) dK [384,512)
   static constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_PT = 192, T_DST = 224, T_DV = 256, T_DK = 384,
                             TMEM_COLS = 512;
 };
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                        const __grid_constant__ CUtensorMap tmDQ, AttnTcParams p, const float2* __restrict__ lsed,
@@ -506,15 +508,15 @@ __global__ void __launch_bounds__(320, 1)
       tc::mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&pds_full[i], 256);
+      tc::mbar_init(&pds_full[i], C::NEW);
       tc::mbar_init(&pds_empty[i], 1);
     }
     tc::mbar_init(sdp_full, 1);
     tc::mbar_init(dq_full, 1);
-    tc::mbar_init(dq_empty, 256);
+    tc::mbar_init(dq_empty, C::NEW);
     tc::mbar_init(dkv_full, 1);
-    tc::mbar_init(sdp_empty, 256);
-    tc::mbar_init(stg_full, 256);
+    tc::mbar_init(sdp_empty, C::NEW);
+    tc::mbar_init(stg_full, C::NEW);
     tc::mbar_init(stg_free, 1);
     tc::mbar_init(ptm_empty, 1);
     *abort_flag = 0;
@@ -572,26 +574,26 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t IDESC_KV = tc::idesc_f16(128, C::D, BF16, false, true);     // P^T dO, dS^T Q: B MN-major
       constexpr uint32_t IDESC_DQ = tc::idesc_f16(128, C::BQ, BF16, true, true);     // K^T dS^T: A, B MN-major
       const uint32_t k_addr = tc::smem_u32(smem + C::OFF_K), v_addr = tc::smem_u32(smem + C::OFF_V);
+      const tc::SDesc kd = tc::sdesc_parts(k_addr, 16, 1024), vd = tc::sdesc_parts(v_addr, 16, 1024);
+      const tc::SDesc ktd = tc::sdesc_parts(k_addr, C::BKV * 128, 1024);  // K^T view (MN-major A of dQ^T)
       bool ok = tc::mbar_wait(kv_full, 0, p.err);
       auto issue_sdp = [&](int i) -> bool {
         const int s = i % QS;
         if (!tc::mbar_wait(&q_full[s], (uint32_t)((i / QS) & 1), p.err)) return false;
         tc::tc_fence_after();
-        const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES);
-        const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES);
+        const tc::SDesc qd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_Q + s * C::QT_BYTES), 16, 1024);
+        const tc::SDesc dod = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_DO + s * C::QT_BYTES), 16, 1024);
 #pragma unroll
         for (int k = 0; k < C::D / 16; ++k) {
           const uint32_t ka = (k >> 2) * (C::BKV * 128) + (k & 3) * 32;
           const uint32_t qa = (k >> 2) * (C::BQ * 128) + (k & 3) * 32;
-          tc::mma_f16_ss(tbase + C::T_S, tc::sdesc_sw128(k_addr + ka, 16, 1024), tc::sdesc_sw128(q_addr + qa, 16, 1024),
-                         IDESC_SDP, k > 0 ? 1u : 0u);
+          tc::mma_f16_ss(tbase + C::T_S, tc::sdesc_at(kd, ka), tc::sdesc_at(qd, qa), IDESC_SDP, k > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int k = 0; k < C::D / 16; ++k) {
           const uint32_t ka = (k >> 2) * (C::BKV * 128) + (k & 3) * 32;
           const uint32_t qa = (k >> 2) * (C::BQ * 128) + (k & 3) * 32;
-          tc::mma_f16_ss(tbase + C::T_DP, tc::sdesc_sw128(v_addr + ka, 16, 1024), tc::sdesc_sw128(do_addr + qa, 16, 1024),
-                         IDESC_SDP, k > 0 ? 1u : 0u);
+          tc::mma_f16_ss(tbase + C::T_DP, tc::sdesc_at(vd, ka), tc::sdesc_at(dod, qa), IDESC_SDP, k > 0 ? 1u : 0u);
         }
         tc::mma_commit(sdp_full);
         return true;
@@ -607,18 +609,17 @@ __global__ void __launch_bounds__(320, 1)
         if (i + 1 < ntile && !issue_sdp(i + 1)) { ok = false; break; }
         if (!tc::mbar_wait(&pds_full[s], ph, p.err)) { ok = false; break; }
         tc::tc_fence_after();
-        const uint32_t q_addr = tc::smem_u32(smem + C::OFF_Q + qs * C::QT_BYTES);
-        const uint32_t do_addr = tc::smem_u32(smem + C::OFF_DO + qs * C::QT_BYTES);
-        const uint32_t ds_addr = tc::smem_u32(smem + C::OFF_DS + s * C::PT_BYTES);
+        const tc::SDesc qmd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_Q + qs * C::QT_BYTES), C::BQ * 128, 1024);
+        const tc::SDesc domd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_DO + qs * C::QT_BYTES), C::BQ * 128, 1024);
+        const tc::SDesc dsd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_DS + s * C::PT_BYTES), 8192, 1024);
+        const uint32_t acc0 = i > 0 ? 1u : 0u;
         // dV += P^T dO ; dK += dS^T Q   (M = 128 keys, N = D, K = 64 queries; A from TMEM)
 #pragma unroll
         for (int k = 0; k < C::BQ / 16; ++k)
-          tc::mma_f16_ts(tbase + C::T_DV, tbase + C::T_PT + k * 8, tc::sdesc_sw128(do_addr + k * 2048, C::BQ * 128, 1024),
-                         IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tbase + C::T_DV, tbase + C::T_PT + k * 8, tc::sdesc_at(domd, k * 2048), IDESC_KV, k > 0 ? 1u : acc0);
 #pragma unroll
         for (int k = 0; k < C::BQ / 16; ++k)
-          tc::mma_f16_ts(tbase + C::T_DK, tbase + C::T_DST + k * 8, tc::sdesc_sw128(q_addr + k * 2048, C::BQ * 128, 1024),
-                         IDESC_KV, (i > 0 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tbase + C::T_DK, tbase + C::T_DST + k * 8, tc::sdesc_at(qmd, k * 2048), IDESC_KV, k > 0 ? 1u : acc0);
         tc::mma_commit(&q_empty[qs]);
         tc::mma_commit(ptm_empty);
         // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
@@ -626,8 +627,7 @@ __global__ void __launch_bounds__(320, 1)
         tc::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < C::BKV / 16; ++k)
-          tc::mma_f16_ss(tbase + C::T_DQ, tc::sdesc_sw128(k_addr + k * 2048, C::BKV * 128, 1024),
-                         tc::sdesc_sw128(ds_addr + k * 2048, 8192, 1024), IDESC_DQ, k > 0 ? 1u : 0u);
+          tc::mma_f16_ss(tbase + C::T_DQ, tc::sdesc_at(ktd, k * 2048), tc::sdesc_at(dsd, k * 2048), IDESC_DQ, k > 0 ? 1u : 0u);
         tc::mma_commit(dq_full);
         tc::mma_commit(&pds_empty[s]);
       }
@@ -635,8 +635,10 @@ __global__ void __launch_bounds__(320, 1)
       else *abort_flag = 1;
     }
   } else {
-    // ---------------- warps 2..9: P^T / dS^T, dQ drain, dK/dV epilogue ----------------
-    // thread = key row r (TMEM lane; also d for dQ^T); group g owns query columns [32g, 32g+32)
+    // ---------------- warps 2..: P^T / dS^T, dQ drain, dK/dV epilogue ----------------
+    // thread = key row r (TMEM lane; also d for dQ^T); group g owns query columns [16g, 16g+16).
+    // NG groups of 4 warps keep enough independent work in flight to hide TMEM / MUFU latency.
+    constexpr int QPG = C::QPG;
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -644,18 +646,18 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     // dQ^T_i (fp32, [d][64 queries]) leaves TMEM through a shared-memory staging tile and is added to
     // the accumulator tile [bh][i][d][64] by two TMA reductions performed in L2 (one per 32-query
-    // half), issued by thread ew == 0: no per-thread atomics. The scale is applied at conversion.
-    const int ew = threadIdx.x - 64;  // 0..255
+    // box), issued by thread ew == 0: no per-thread atomics. The scale is applied at conversion.
+    const int ew = threadIdx.x - 64;  // 0 .. NEW-1
     uint8_t* stg = smem + C::OFF_STG;
     const int64_t ntq = sq_pad / C::BQ;
     auto drain_dq = [&](int i) -> bool {
       if (!tc::mbar_wait(dq_full, (uint32_t)(i & 1), p.err)) return false;
       tc::tc_fence_after();
-      uint32_t v[32];
+      uint32_t v[QPG];
       __syncwarp();
-      tc::tmem_ld32(tbase + C::T_DQ + g * 32 + lane_off, v);
+      tc::tmem_ld16(tbase + C::T_DQ + g * QPG + lane_off, v);
       tc::tmem_wait_ld();
-      tc::reg_fence32(v);
+      tc::reg_fence16(v);
       tc::tc_fence_before();
       tc::mbar_arrive(dq_empty);
       if (i > 0) {
@@ -665,11 +667,13 @@ __global__ void __launch_bounds__(320, 1)
         }
         if (!tc::mbar_wait(stg_free, (uint32_t)((i - 1) & 1), p.err)) return false;
       }
-      // box g, row d = r: 8 16-byte chunks at their 128-byte-swizzle positions (conflict-free)
-      uint8_t* row = stg + g * (C::D * 128) + r * 128;
+      // box g/2 (32 queries), row d = r: 4 16-byte chunks at their 128-byte-swizzle positions
+      uint8_t* row = stg + (g >> 1) * (C::D * 128) + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      for (int c = 0; c < 4; ++c) {
+        const int cc = (g & 1) * 4 + c;
+        *reinterpret_cast<uint4*>(row + ((cc ^ (r & 7)) << 4)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      }
       tc::fence_async_shared();
       tc::mbar_arrive(stg_full);
       if (ew == 0) {
@@ -689,42 +693,42 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc::tc_fence_after();
-      uint32_t sv[32], dp[32];
+      uint32_t sv[QPG], dp[QPG];
       __syncwarp();
-      tc::tmem_ld32(tbase + C::T_S + g * 32 + lane_off, sv);
-      tc::tmem_ld32(tbase + C::T_DP + g * 32 + lane_off, dp);
+      tc::tmem_ld16(tbase + C::T_S + g * QPG + lane_off, sv);
+      tc::tmem_ld16(tbase + C::T_DP + g * QPG + lane_off, dp);
       tc::tmem_wait_ld();
+      tc::reg_fence16(sv);
+      tc::reg_fence16(dp);
       tc::tc_fence_before();
       tc::mbar_arrive(sdp_empty);
-      const float2* ld = reinterpret_cast<const float2*>(smem + C::OFF_LD + qs * C::LD_BYTES) + g * 32;
-      uint32_t wp[16], wd[16];
+      // (lse * log2e, delta) of two queries per 16-byte load; padding rows hold (+inf, 0)
+      const float4* ld = reinterpret_cast<const float4*>(smem + C::OFF_LD + qs * C::LD_BYTES) + g * (QPG / 2);
+      uint32_t wp[QPG / 2], wd[QPG / 2];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        float pv[2], dv[2];
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int c = 2 * e + t;
-          const float2 L = ld[c];  // (lse * log2e, delta); padding rows hold (+inf, 0)
-          const float pp = ex2(__uint_as_float(sv[c]) * p.scale_log2 - L.x);
-          pv[t] = pp;
-          dv[t] = pp * (__uint_as_float(dp[c]) - L.y);
-        }
-        wp[e] = pack2(pv[0], pv[1], BF16);
-        wd[e] = pack2(dv[0], dv[1], BF16);
+      for (int e = 0; e < QPG / 2; ++e) {
+        const float4 L = ld[e];
+        const float p0 = ex2(fmaf(__uint_as_float(sv[2 * e]), p.scale_log2, -L.x));
+        const float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), p.scale_log2, -L.z));
+        const float2 ds = __fmul2_rn(make_float2(p0, p1), __fadd2_rn(make_float2(__uint_as_float(dp[2 * e]),
+                                                                                 __uint_as_float(dp[2 * e + 1])),
+                                                                     make_float2(-L.y, -L.w)));
+        wp[e] = pack2(p0, p1, BF16);
+        wd[e] = pack2(ds.x, ds.y, BF16);
       }
       // P^T / dS^T in TMEM were read by the dV / dK MMAs of tile i-1
       if (i >= 1 && !tc::mbar_wait(ptm_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
       tc::tc_fence_after();
-      tc::tmem_st16(tbase + C::T_PT + g * 16 + lane_off, wp);
-      tc::tmem_st16(tbase + C::T_DST + g * 16 + lane_off, wd);
+      tc::tmem_st8(tbase + C::T_PT + g * (QPG / 2) + lane_off, wp);
+      tc::tmem_st8(tbase + C::T_DST + g * (QPG / 2) + lane_off, wd);
       // dS^T buffer s in shared memory was last read by the dQ^T MMA of tile i-2
       if (i >= 2 && !tc::mbar_wait(&pds_empty[s], (uint32_t)(((i - 2) >> 1) & 1), p.err)) { ok = false; break; }
       uint8_t* dst = smem + C::OFF_DS + s * C::PT_BYTES + r * 128;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {  // 4 granules of 8 queries, 128-byte swizzled rows
-        const int gr = g * 4 + q4;
+      for (int q2 = 0; q2 < QPG / 8; ++q2) {  // granules of 8 queries, 128-byte swizzled rows
+        const int gr = g * (QPG / 8) + q2;
         *reinterpret_cast<uint4*>(dst + ((gr ^ (r & 7)) << 4)) =
-            make_uint4(wd[4 * q4], wd[4 * q4 + 1], wd[4 * q4 + 2], wd[4 * q4 + 3]);
+            make_uint4(wd[4 * q2], wd[4 * q2 + 1], wd[4 * q2 + 2], wd[4 * q2 + 3]);
       }
       tc::tmem_wait_st();
       tc::fence_async_shared();
@@ -734,7 +738,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     if (ok && ntile > 0) ok = drain_dq(ntile - 1);
     if (ew == 0) tc::bulk_wait0();
-    // ---------------- dK, dV epilogue: group g writes d columns [64g, 64g+64) ----------------
+    // ---------------- dK, dV epilogue: group g writes d columns [32g, 32g+32) ----------------
     if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
       tc::tc_fence_after();
       const int64_t krow = k0 + r;
@@ -743,23 +747,20 @@ __global__ void __launch_bounds__(320, 1)
         const int64_t* st = which ? p.dk_s : p.dv_s;
         const float mul = which ? p.scale : 1.f;
         const uint32_t tcol = which ? C::T_DK : C::T_DV;
+        uint32_t v[32];
+        __syncwarp();
+        tc::tmem_ld32(tbase + tcol + g * 32 + lane_off, v);
+        tc::tmem_wait_ld();
+        tc::reg_fence32(v);
+        if (base && krow < p.Sk) {
+          uint32_t w[16];
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = g * 2 + cc;
-          uint32_t v[32];
-          __syncwarp();
-          tc::tmem_ld32(tbase + tcol + c * 32 + lane_off, v);
-          tc::tmem_wait_ld();
-          if (base && krow < p.Sk) {
-            uint32_t w[16];
+          for (int e = 0; e < 16; ++e)
+            w[e] = pack2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul, BF16);
+          uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + (int64_t)b * st[0] +
+                                               (int64_t)h * st[1] + krow * st[2] + g * 32);
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              w[e] = pack2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul, BF16);
-            uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + (int64_t)b * st[0] +
-                                                 (int64_t)h * st[1] + krow * st[2] + c * 32);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
-          }
+          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         }
       }
     } else {

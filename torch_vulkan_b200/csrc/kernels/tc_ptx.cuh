@@ -218,6 +218,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+// 32 lanes x 8 columns store.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 // 32 lanes x 32 columns store.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
   asm volatile(
@@ -240,6 +246,22 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   d |= 1ull << 46;
   d |= 2ull << 61;
   return d;
+}
+
+// The same descriptor split in two words. The 14-bit start-address field sits in the low word and a
+// CTA's shared memory lies below 256 KB, so stepping through a tile is one 32-bit add of
+// (byte offset >> 4) with no carry: the MMA-issuing thread spends one instruction per operand.
+struct SDesc {
+  uint32_t lo, hi;
+};
+__device__ __forceinline__ SDesc sdesc_parts(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  SDesc d;
+  d.lo = ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+  d.hi = ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);  // version 1 (bit 46), 128B swizzle (61..63)
+  return d;
+}
+__device__ __forceinline__ uint64_t sdesc_at(SDesc d, uint32_t byte_off) {
+  return ((uint64_t)d.hi << 32) | (uint64_t)(d.lo + (byte_off >> 4));
 }
 
 // Instruction descriptor for kind::f16 with fp32 accumulation.
