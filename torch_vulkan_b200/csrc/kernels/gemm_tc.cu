@@ -95,8 +95,11 @@ struct Cfg {
   static constexpr int R_BYTES = DEQ ? BN * BK : 0;  // raw int8 tile
   static constexpr int STAGE = A_BYTES + B_BYTES + R_BYTES;
   static constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  // int8 dequant warps run pure ALU work; they take warp ids 6-8, 10-12, 14-15 so that none shares
+  // a scheduler (warp id % 4) with the MMA-issuing warp 1, whose issue slots they would otherwise
+  // take (warps 9 and 13 idle).
   static constexpr int DEQ_WARPS = DEQ ? 8 : 0;
-  static constexpr int THREADS = (6 + DEQ_WARPS) * 32;
+  static constexpr int THREADS = DEQ ? 16 * 32 : 6 * 32;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr uint32_t SUB_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per M sub-tile
   static constexpr uint32_t ACC_COLS = MSUB * SUB_COLS;  // one accumulator (all M sub-tiles)
@@ -257,6 +260,10 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC_BASE = tc::idesc_f16(BM, BN, BF16, false, false);
       const uint32_t idesc = IDESC_BASE | ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16);
+      // K-major: +32 B per 16-element K step inside the 128 B swizzle row (LBO unused);
+      // MN-major: +16 rows of 128 B per step, LBO = distance between 64-element MN chunks.
+      const uint32_t a_step = p.a_mn ? 2048u : 32u, b_step = p.b_mn ? 2048u : 32u;
+      const uint32_t a_lbo = p.a_mn ? 8192u : 16u, b_lbo = p.b_mn ? 8192u : 16u;
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -277,20 +284,16 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           tc::tc_fence_after();
           uint8_t* sa = smem + stage * C::STAGE;
           uint8_t* sb = sa + C::A_BYTES;
-          const uint32_t a_addr = tc::smem_u32(sa), b_addr = tc::smem_u32(sb);
+          const tc::SDesc ad0 = tc::sdesc_parts(tc::smem_u32(sa), a_lbo, 1024);
+          const tc::SDesc bd0 = tc::sdesc_parts(tc::smem_u32(sb), b_lbo, 1024);
+          const uint32_t acc0 = kb > 0 ? 1u : 0u;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // K-major: +32 B per 16-element K step inside the 128 B swizzle row.
-            // MN-major: +16 rows of 128 B per step; LBO = distance between 64-element MN chunks.
-            const uint64_t bd = p.b_mn ? tc::sdesc_sw128(b_addr + k * 2048, 8192, 1024)
-                                       : tc::sdesc_sw128(b_addr + k * 32, 16, 1024);
+            const uint64_t bd = tc::sdesc_at(bd0, k * b_step);
 #pragma unroll
-            for (int ms = 0; ms < MSUB; ++ms) {
-              // M sub-tile ms: K-major rows 128*ms.. at +ms*16 KB; MN-major chunks 2ms, 2ms+1 at +ms*16 KB
-              const uint64_t ad = p.a_mn ? tc::sdesc_sw128(a_addr + ms * 16384 + k * 2048, 8192, 1024)
-                                         : tc::sdesc_sw128(a_addr + ms * 16384 + k * 32, 16, 1024);
-              tc::mma_f16_ss(d + ms * C::SUB_COLS, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-            }
+            for (int ms = 0; ms < MSUB; ++ms)  // M sub-tile ms at +ms*16 KB (K-major rows / MN-major chunks)
+              tc::mma_f16_ss(d + ms * C::SUB_COLS, tc::sdesc_at(ad0, ms * 16384 + k * a_step), bd, idesc,
+                             k > 0 ? 1u : acc0);
           }
           tc::mma_commit(&empty[stage]);
           if (++stage == S) {
@@ -356,9 +359,10 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       tc::tc_fence_before();
       tc::mbar_arrive(&tempty[acc]);
     }
-  } else if (DEQ) {
+  } else if (DEQ && (warp & 3) != 1) {
     // ------------------------------- int8 dequant -------------------------------------------
-    const int dt = threadIdx.x - 6 * 32;  // 0 .. NDQ-1
+    const int dw = warp - 6 - (warp > 9 ? 1 : 0) - (warp > 13 ? 1 : 0);  // 0 .. 7
+    const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
