@@ -59,6 +59,38 @@ struct VecIO<__nv_bfloat16, 8> : VecIO16<__nv_bfloat16> {};
 template <>
 struct VecIO<__half, 8> : VecIO16<__half> {};
 
+// A vector kept in its stored form until it is needed, so that a load can stay in flight across
+// other work (16-byte vectors: one uint4; otherwise converted on load).
+template <typename T, int V>
+struct RawVec {
+  float v[V];
+  __device__ __forceinline__ void load(const T* p) { VecIO<T, V>::load(p, v); }
+  __device__ __forceinline__ void get(float* o) const {
+#pragma unroll
+    for (int i = 0; i < V; ++i) o[i] = v[i];
+  }
+};
+template <typename T>
+struct RawVec16 {
+  uint4 r;
+  __device__ __forceinline__ void load(const T* p) { r = *reinterpret_cast<const uint4*>(p); }
+  __device__ __forceinline__ void get(float* o) const {
+    const T* h = reinterpret_cast<const T*>(&r);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = to_f32(h[i]);
+  }
+};
+template <>
+struct RawVec<__nv_bfloat16, 8> : RawVec16<__nv_bfloat16> {};
+template <>
+struct RawVec<__half, 8> : RawVec16<__half> {};
+template <>
+struct RawVec<float, 4> {
+  float4 r;
+  __device__ __forceinline__ void load(const float* p) { r = *reinterpret_cast<const float4*>(p); }
+  __device__ __forceinline__ void get(float* o) const { o[0] = r.x, o[1] = r.y, o[2] = r.z, o[3] = r.w; }
+};
+
 template <int GROUP>
 __device__ __forceinline__ float group_sum(float v, float* red) {
   if (GROUP == 32) return warp_sum(v);
@@ -410,29 +442,47 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
   const int rpb = blockDim.x / GROUP;
   const int t = threadIdx.x % GROUP;
   const float invD = 1.f / (float)D;
-  float pdw[NCH][V], pdb[NCH][V];
+  const int64_t stride = (int64_t)gridDim.x * rpb;
+  float pdw[NCH][V], pdb[NCH][V], wv[NCH][V];
 #pragma unroll
-  for (int c = 0; c < NCH; ++c)
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t idx = ((int64_t)c * GROUP + t) * V;
 #pragma unroll
-    for (int i = 0; i < V; ++i) pdw[c][i] = pdb[c][i] = 0.f;
-  for (int64_t row = (int64_t)blockIdx.x * rpb + threadIdx.x / GROUP; row - threadIdx.x / GROUP < rows;
-       row += (int64_t)gridDim.x * rpb) {
+    for (int i = 0; i < V; ++i) pdw[c][i] = pdb[c][i] = 0.f, wv[c][i] = 1.f;
+    if (w && idx < D) VecIO<T, V>::load(w + idx, wv[c]);
+  }
+  // the next row's x and g are loaded (and stay in flight) while the current row is reduced
+  RawVec<T, V> nx[NCH], ng[NCH];
+  float nmu = 0.f, nrs = 0.f;
+  int64_t row = (int64_t)blockIdx.x * rpb + threadIdx.x / GROUP;
+  auto fetch = [&](int64_t r) {
+    if (r < rows) nmu = mean[r], nrs = rstd[r];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t idx = ((int64_t)c * GROUP + t) * V;
+      if (r < rows && idx < D) {
+        nx[c].load(x + r * D + idx);
+        ng[c].load(g + r * D + idx);
+      }
+    }
+  };
+  fetch(row);
+  for (; row - threadIdx.x / GROUP < rows; row += stride) {
     const bool active = row < rows;
     float xh[NCH][V], gw[NCH][V];
     float s1 = 0.f, s2 = 0.f;
-    const float mu = active ? mean[row] : 0.f, rs = active ? rstd[row] : 0.f;
+    const float mu = nmu, rs = nrs;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      int64_t idx = ((int64_t)c * GROUP + t) * V;
+      const int64_t idx = ((int64_t)c * GROUP + t) * V;
       if (active && idx < D) {
-        float gv[V], wv[V];
-        VecIO<T, V>::load(x + row * D + idx, xh[c]);
-        VecIO<T, V>::load(g + row * D + idx, gv);
-        if (w) VecIO<T, V>::load(w + idx, wv);
+        float gv[V];
+        nx[c].get(xh[c]);
+        ng[c].get(gv);
 #pragma unroll
         for (int i = 0; i < V; ++i) {
           xh[c][i] = (xh[c][i] - mu) * rs;
-          gw[c][i] = w ? gv[i] * wv[i] : gv[i];
+          gw[c][i] = gv[i] * wv[c][i];
           s1 += gw[c][i];
           s2 += gw[c][i] * xh[c][i];
           pdw[c][i] += gv[i] * xh[c][i];
@@ -440,12 +490,13 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
         }
       }
     }
+    fetch(row + stride);
     s1 = group_sum<GROUP>(s1, red) * invD;
     s2 = group_sum<GROUP>(s2, red) * invD;
     if (!active || !dx) continue;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      int64_t idx = ((int64_t)c * GROUP + t) * V;
+      const int64_t idx = ((int64_t)c * GROUP + t) * V;
       if (idx < D) {
         float o[V];
 #pragma unroll
@@ -471,28 +522,40 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
 }
 
 // Column sum of the partials: dw[d] = sum_s part[s][d], db[d] = sum_s part[s][D + d].
+// blockDim = (32, 32): x over 32 consecutive columns (128-byte loads per slot), y over the slots;
+// the 32 slot lanes are combined through shared memory.
 template <typename T>
-__global__ void ln_wgrad_reduce(const float* __restrict__ part, int64_t nslots, int64_t D, T* __restrict__ dw,
-                                T* __restrict__ db) {
-  // blockDim = (32, 8): x over columns, y splits the slots; combine through shared memory.
-  __shared__ float sw[8][33], sb[8][33];
-  int64_t col = (int64_t)blockIdx.x * 32 + threadIdx.x;
-  float aw = 0.f, ab = 0.f;
-  if (col < D)
-    for (int64_t s = threadIdx.y; s < nslots; s += 8) {
-      aw += part[s * 2 * D + col];
-      ab += part[s * 2 * D + D + col];
+__global__ void __launch_bounds__(1024) ln_wgrad_reduce(const float* __restrict__ part, int64_t nslots, int64_t D,
+                                                        T* __restrict__ dw, T* __restrict__ db) {
+  __shared__ float sw[32][33], sb[32][33];
+  const int64_t col = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  float aw0 = 0.f, ab0 = 0.f, aw1 = 0.f, ab1 = 0.f;
+  if (col < D) {
+    int64_t s = threadIdx.y;
+    for (; s + 32 < nslots; s += 64) {
+      aw0 += part[s * 2 * D + col];
+      ab0 += part[s * 2 * D + D + col];
+      aw1 += part[(s + 32) * 2 * D + col];
+      ab1 += part[(s + 32) * 2 * D + D + col];
     }
-  sw[threadIdx.y][threadIdx.x] = aw;
-  sb[threadIdx.y][threadIdx.x] = ab;
+    if (s < nslots) {
+      aw0 += part[s * 2 * D + col];
+      ab0 += part[s * 2 * D + D + col];
+    }
+  }
+  sw[threadIdx.y][threadIdx.x] = aw0 + aw1;
+  sb[threadIdx.y][threadIdx.x] = ab0 + ab1;
   __syncthreads();
-  if (threadIdx.y == 0 && col < D) {
-    for (int k = 1; k < 8; ++k) {
-      aw += sw[k][threadIdx.x];
-      ab += sb[k][threadIdx.x];
+  for (int k = 16; k > 0; k >>= 1) {
+    if (threadIdx.y < k) {
+      sw[threadIdx.y][threadIdx.x] += sw[threadIdx.y + k][threadIdx.x];
+      sb[threadIdx.y][threadIdx.x] += sb[threadIdx.y + k][threadIdx.x];
     }
-    if (dw) dw[col] = from_f32<T>(aw);
-    if (db) db[col] = from_f32<T>(ab);
+    __syncthreads();
+  }
+  if (threadIdx.y == 0 && col < D) {
+    if (dw) dw[col] = from_f32<T>(sw[0][threadIdx.x]);
+    if (db) db[col] = from_f32<T>(sb[0][threadIdx.x]);
   }
 }
 
@@ -579,7 +642,7 @@ struct LnPlan {
   int64_t nslots;  // partial slots (rows of the workspace)
 };
 
-LnPlan ln_plan(const b2_layernorm_args* a) {
+LnPlan ln_plan(const b2_layernorm_args* a, bool fwd) {
   LnPlan p{};
   const int V = dtype_size(a->dtype) == 4 ? 4 : 8;
   bool vec = (a->D % V == 0);
@@ -610,8 +673,9 @@ LnPlan ln_plan(const b2_layernorm_args* a) {
   if (p.kind == 0) {
     const int rpb = 256 / p.group;
     int64_t blocks = (a->rows + rpb - 1) / rpb;
-    // enough blocks to fill the GPU; each row group then walks several rows (fewer partial slots)
-    int64_t cap = (int64_t)sms * (p.group == 32 ? 4 : 4);
+    // forward: enough blocks to fill the GPU. backward: two blocks per SM walking several rows with
+    // the next row prefetched, which keeps the weight-gradient partial slots (and their reduction) few
+    int64_t cap = fwd ? (int64_t)sms * 4 : (p.group == 32 ? (int64_t)sms / 2 : (int64_t)sms * 2);
     p.grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
     p.nslots = (int64_t)p.grid * rpb;
   } else {
@@ -649,7 +713,7 @@ void ln_reg_switch(const b2_layernorm_args* a, const LnPlan& p, cudaStream_t st,
 
 template <typename T>
 int ln_run(const b2_layernorm_args* a, cudaStream_t st, bool fwd) {
-  LnPlan p = ln_plan(a);
+  LnPlan p = ln_plan(a, fwd);
   constexpr int VV = sizeof(T) == 4 ? 4 : 8;
   const bool want_w = !fwd && (a->dw || a->db);
   float* part = want_w ? (float*)a->workspace : nullptr;
@@ -678,7 +742,7 @@ int ln_run(const b2_layernorm_args* a, cudaStream_t st, bool fwd) {
   }
   if (want_w) {
     LaunchScope ls("layernorm_wgrad_reduce", st);
-    dim3 block(32, 8);
+    dim3 block(32, 32);
     ln_wgrad_reduce<T><<<(unsigned)((a->D + 31) / 32), block, 0, st>>>(part, p.nslots, a->D, (T*)a->dw, (T*)a->db);
   }
   return after_launch(fwd ? "b2_layernorm_fwd" : "b2_layernorm_bwd");
@@ -757,7 +821,7 @@ int ln_bwd_planned(const b2_layernorm_args* a, const LnPlan& p, float* part, cud
   }
   if (want_w) {
     LaunchScope ls("layernorm_wgrad_reduce_noalloc", st);
-    dim3 block(32, 8);
+    dim3 block(32, 32);
     ln_wgrad_reduce<T><<<(unsigned)((a->D + 31) / 32), block, 0, st>>>(pw, p.nslots, a->D, (T*)a->dw, (T*)a->db);
   }
   return after_launch("b2_layernorm_bwd_noalloc");
@@ -784,7 +848,7 @@ int b2_layernorm_bwd_noalloc(const b2_layernorm_args* a, b2_stream_t stream) {
   if ((a->dw || a->db) && max_slots < 1)
     return fail(B2_ERR_ARG, "layernorm_bwd_noalloc: D = " + std::to_string(a->D) + " exceeds the static scratch (D <= " +
                                 std::to_string(kLnNoAllocScratchFloats / 2) + ")");
-  LnPlan p = ln_plan(a);
+  LnPlan p = ln_plan(a, false);
   if (a->dw || a->db) {
     if (p.kind == 0) {
       const int rpb = 256 / p.group;
@@ -809,7 +873,7 @@ int b2_layernorm_bwd_noalloc(const b2_layernorm_args* a, b2_stream_t stream) {
 uint64_t b2_layernorm_bwd_workspace_bytes(const b2_layernorm_args* a) {
   if (!a || a->rows <= 0 || a->D <= 0) return 0;
   if (ensure_init()) return 0;
-  LnPlan p = ln_plan(a);
+  LnPlan p = ln_plan(a, false);
   return (uint64_t)p.nslots * 2 * (uint64_t)a->D * sizeof(float);
 }
 }
