@@ -365,6 +365,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
     int stage = 0;
     uint32_t phase = 0;
+    constexpr int FIPT = (BN * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
+    float fsc[FIPT];
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       int m0, n0, b;
       tile_coords(t, m0, n0, b);
@@ -379,14 +381,25 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         if (!p.b_mn) {
           // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
-          for (int i = dt; i < BN * 4; i += NDQ) {
+          // block-64 scales change with the K block; per-row scales were loaded once for the tile
+          if (p.scale_layout == 0 || kb == 0) {
+#pragma unroll
+            for (int u = 0; u < FIPT; ++u) {  // every scale load in flight before the first is used
+              const int i = dt + u * NDQ;
+              const int64_t gn = (int64_t)n0 + (i >> 2);
+              fsc[u] = 0.f;
+              if (i < BN * 4 && gn < p.deq_rows)
+                fsc[u] = p.scale_layout == 0
+                             ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
+                             : reinterpret_cast<const float*>(p.scale)[gn];
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < FIPT; ++u) {
+            const int i = dt + u * NDQ;
+            if (i >= BN * 4) break;
             const int n = i >> 2, j = i & 3;  // 16 int8 = k 16j..16j+15
-            const int64_t gn = (int64_t)n0 + n;
-            float s = 0.f;
-            if (gn < p.deq_rows)
-              s = p.scale_layout == 0
-                      ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
-                      : reinterpret_cast<const float*>(p.scale)[gn];
+            const float s = fsc[u];
             const int4 raw = *reinterpret_cast<const int4*>(sr + n * 64 + j * 16);
             uint32_t w[8];
             dequant16(raw, s, w);
@@ -398,15 +411,26 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         } else {
           // backward: raw [64 rows i (n_feat)][BN bytes (k_feat = n_gemm)]; B stage MN-major SW128:
           // chunk j = n_gemm/64 at j*8192, row i at i*128, 16 B granule g at ((g ^ (i & 7)) * 16).
-          for (int e = dt; e < 64 * (BN / 16); e += NDQ) {
+          constexpr int IPT = (64 * (BN / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // items per thread
+          float sc[IPT];
+#pragma unroll
+          for (int u = 0; u < IPT; ++u) {  // every scale load in flight before the first is used
+            const int e = dt + u * NDQ;
             const int i = e / (BN / 16), qd = e % (BN / 16);
             const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
             const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
-            float s = 0.f;
-            if (nf < p.deq_rows)
-              s = p.scale_layout == 0
-                      ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
-                      : reinterpret_cast<const float*>(p.scale)[nf];
+            sc[u] = 0.f;
+            if (e < 64 * (BN / 16) && nf < p.deq_rows)
+              sc[u] = p.scale_layout == 0
+                          ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
+                          : reinterpret_cast<const float*>(p.scale)[nf];
+          }
+#pragma unroll
+          for (int u = 0; u < IPT; ++u) {
+            const int e = dt + u * NDQ;
+            if (e >= 64 * (BN / 16)) break;
+            const int i = e / (BN / 16), qd = e % (BN / 16);
+            const float s = sc[u];
             const int4 raw = *reinterpret_cast<const int4*>(sr + i * BN + qd * 16);
             uint32_t w[8];
             dequant16(raw, s, w);
