@@ -372,7 +372,7 @@ def run_dit(dev, world, blocks, tokens, steps, warmup):
 
     rank = dist.get_rank() if world > 1 else 0
     model = DiTStack(blocks=blocks, seed=0, device=dev)  # identical replicas on every rank
-    trainer = LoRATrainer(model, lr=1e-4)
+    trainer = LoRATrainer(model, lr=1e-4, fused_optimizer=True)
     batch = synthetic_batch(tokens=tokens, seed=1000 + rank, device=dev)  # each rank its own sample
     for _ in range(warmup):
         trainer.step(*batch)
@@ -394,7 +394,8 @@ def run_dit(dev, world, blocks, tokens, steps, warmup):
     out = {"blocks": blocks, "tokens": tokens, "samples_per_step": world, "ms_per_step": round(ms, 3),
            "samples_per_s": round(world / (ms * 1e-3), 2), "tflops": round(step_flops / (ms * 1e-3) / 1e12, 1),
            "loss": float(loss.item()), "lora_params": sum(p.numel() for p in trainer.params),
-           "allreduce": "bucketed per block, NCCL AVG, overlapped with backward" if world > 1 else None}
+           "allreduce": "bucketed per block, NCCL AVG, overlapped with backward" if world > 1 else None,
+           "optimizer": "multi-tensor AdamW kernel (the arithmetic of AdamW foreach=False)"}
     del trainer, model
     torch.cuda.empty_cache()
     return out
@@ -556,7 +557,7 @@ def run_case(name, iters):
     else:  # one DiT block LoRA step
         from torch_vulkan_b200.dit import DiTStack, LoRATrainer, synthetic_batch
 
-        trainer = LoRATrainer(DiTStack(blocks=1, seed=0, device=dev))
+        trainer = LoRATrainer(DiTStack(blocks=1, seed=0, device=dev), fused_optimizer=True)
         batch = synthetic_batch(tokens=1024, device=dev)
         fn = lambda: trainer.step(*batch)  # noqa: E731
     for _ in range(iters):

@@ -163,8 +163,14 @@ typedef struct b2_gemm_args {
   int32_t has_bias;
   int32_t force_simt; /* 1: always use the SIMT kernel (A/B switch, like set_coop_enabled) */
   int32_t pad_;
+  /* Optional scratch for split-K (GEMMs with few output tiles and a long K): at least
+   * b2_gemm_workspace_bytes(args) bytes, 16-byte aligned. NULL or too small: no split. */
+  void* workspace;
+  int64_t workspace_bytes;
 } b2_gemm_args;
 int b2_gemm(const b2_gemm_args* args, b2_stream_t stream);
+/* Scratch bytes b2_gemm would use for these arguments (0: none). */
+uint64_t b2_gemm_workspace_bytes(const b2_gemm_args* args);
 /* Which kernel b2_gemm would pick for these arguments: 0 = SIMT, 1 = tcgen05. */
 int b2_gemm_path(const b2_gemm_args* args);
 

@@ -76,3 +76,32 @@ def test_adamw_matches_cpu(tv, dt):
     assert max(abs(a - b) / max(abs(a), 1e-6) for a, b in zip(cpu, gpu)) < tol, (cpu, gpu)
     kc = tv.kernel_counts()
     assert kc.get("aten::addcmul_", 0) > 0 and kc.get("aten::addcdiv_", 0) > 0 and kc.get("aten::lerp_.Scalar", 0) > 0, kc
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_fused_adamw_matches_foreach_false(tv, dt):
+    """FusedAdamW (one b2_adamw_step launch per 48 tensors) against torch.optim.AdamW(foreach=False)
+    running on this library's addcmul_/addcdiv_/lerp_, over 10 steps of the same gradients."""
+    from torch_vulkan_b200.optim import FusedAdamW
+
+    g = torch.Generator().manual_seed(3)
+    shapes = [(16, 2048), (2048, 16), (7,), (3, 5, 9)] * 13  # 52 tensors: more than one launch chunk
+    init = [torch.randn(s, generator=g).to(dt) for s in shapes]
+    grads = [[torch.randn(s, generator=g).to(dt) for s in shapes] for _ in range(10)]
+
+    def run(make):
+        ps = [torch.nn.Parameter(t.clone().cuda()) for t in init]
+        opt = make(ps)
+        for step in range(10):
+            for p, gr in zip(ps, grads[step]):
+                p.grad = gr.cuda()
+            opt.step()
+        return [p.detach().cpu().float() for p in ps]
+
+    ref = run(lambda ps: torch.optim.AdamW(ps, lr=1e-2, weight_decay=0.01, foreach=False))
+    tv.reset_counts()
+    got = run(lambda ps: FusedAdamW(ps, lr=1e-2, weight_decay=0.01))
+    assert tv.kernel_counts().get("b2::adamw_step_", 0) == 10  # one call (two launches: 48 + 4 tensors) per step
+    tol = 1e-6 if dt == torch.float32 else 1e-2
+    for a, b in zip(got, ref):
+        assert torch.allclose(a, b, rtol=tol, atol=tol), (a - b).abs().max()

@@ -157,3 +157,24 @@ def test_tc_dit_shapes():
         w = rnd_mm((n, k), torch.bfloat16, 8) * 0.02
         out = torch.nn.functional.linear(dev(x), dev(w))
         gemm_check(out, x.double() @ w.double().t(), torch.bfloat16, k)
+
+
+@pytest.mark.parametrize("m,k,n,ta,bias", [(4096, 2048, 16, False, False), (2048, 4096, 16, True, False),
+                                           (16, 4096, 2048, True, True), (200, 3000, 24, False, True)])
+def test_tc_split_k_skinny(_lib, m, k, n, ta, bias):
+    """Few output tiles and a long K (the LoRA projections): split-K partials in a scratch buffer and
+    a reduction kernel; same result as the oracle, alpha/beta/bias applied once."""
+    dt = torch.bfloat16
+    a = rnd_mm((k, m) if ta else (m, k), dt, 21)
+    b = rnd_mm((k, n), dt, 22)
+    ad = dev(a).t() if ta else dev(a)
+    ac = a.t() if ta else a
+    if bias:
+        c = rnd_mm((n,), dt, 23)
+        out = torch.addmm(dev(c), ad, dev(b), beta=0.5, alpha=2.0)
+        ref = oracle.addmm(c, ac, b, alpha=2.0, beta=0.5)
+    else:
+        out = torch.mm(ad, dev(b))
+        ref = oracle.mm(ac, b)
+    gemm_check(out, ref, dt, k)
+    assert _lib.fallback_counts() == {}

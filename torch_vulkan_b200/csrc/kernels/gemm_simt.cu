@@ -11,6 +11,7 @@ namespace b2 {
 
 int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st);  // gemm_tc.cu
 bool gemm_tc_eligible(const b2_gemm_args* a);
+uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a);  // gemm_tc.cu
 
 namespace {
 
@@ -121,6 +122,11 @@ int simt_launch(const b2_gemm_args* a, cudaStream_t st) {
 }  // namespace b2
 
 using namespace b2;
+
+extern "C" uint64_t b2_gemm_workspace_bytes(const b2_gemm_args* a) {
+  if (!a || a->force_simt || ensure_init()) return 0;
+  return a->K > 0 ? gemm_tc_workspace_bytes(a) : 0;
+}
 
 extern "C" int b2_gemm_path(const b2_gemm_args* a) {
   if (!a || a->force_simt) return 0;

@@ -85,6 +85,11 @@ struct TcParams {
   int scale_layout;
   int64_t scale_nb;   // columns of the block-64 scale matrix
   int64_t deq_rows;   // rows of q (output features N of the linear)
+  // split-K: work item t covers tile t % tiles and K blocks [split * kps, split * kps + kps) with
+  // split = t / tiles; its fp32 partial goes to partial[split][M][N] (no alpha / bias) and
+  // gemm_splitk_reduce forms C. ksplit == 1: the epilogue writes C directly.
+  int ksplit, kps;
+  float* partial;
 };
 
 template <int BN, int DEQ, int MSUB>
@@ -161,6 +166,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = p.m_tiles * p.n_tiles * (int)p.batch;
+  const int total_work = total_tiles * p.ksplit;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -184,7 +190,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
+  auto k_range = [&](int t, int& kb0, int& kb1) {
+    kb0 = (t / total_tiles) * p.kps;
+    kb1 = kb0 + p.kps < p.k_blocks ? kb0 + p.kps : p.k_blocks;
+  };
   auto tile_coords = [&](int t, int& m0, int& n0, int& b) {
+    t %= total_tiles;
     int per_b = p.m_tiles * p.n_tiles;
     b = t / per_b;
     int r = t - b * per_b;
@@ -202,10 +213,11 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       uint32_t phase = 0;
       int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        int m0, n0, b;
+      for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x) {
+        int m0, n0, b, kb0, kb1;
         tile_coords(t, m0, n0, b);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        k_range(t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, p.err) || *abort_flag) {
             ok = false;
             *abort_flag = 1;
@@ -268,7 +280,9 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x, ++it) {
+        int kb0, kb1;
+        k_range(t, kb0, kb1);
         const int acc = it & 1;
         if (!tc::mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, p.err) || *abort_flag) {
           ok = false;
@@ -276,7 +290,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         }
         tc::tc_fence_after();
         const uint32_t d = tbase + (uint32_t)(acc * C::ACC_COLS);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, p.err) || (DEQ && !tc::mbar_wait(&bready[stage], phase, p.err))) {
             ok = false;
             break;
@@ -286,7 +300,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           uint8_t* sb = sa + C::A_BYTES;
           const tc::SDesc ad0 = tc::sdesc_parts(tc::smem_u32(sa), a_lbo, 1024);
           const tc::SDesc bd0 = tc::sdesc_parts(tc::smem_u32(sb), b_lbo, 1024);
-          const uint32_t acc0 = kb > 0 ? 1u : 0u;
+          const uint32_t acc0 = kb > kb0 ? 1u : 0u;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t bd = tc::sdesc_at(bd0, k * b_step);
@@ -311,7 +325,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int it = 0;
     using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+    for (int t = blockIdx.x; t < total_work; t += gridDim.x, ++it) {
       const int acc = it & 1;
       if (!tc::mbar_wait(&tfull[acc], (it >> 1) & 1, p.err) || *abort_flag) {
         *abort_flag = 1;
@@ -334,6 +348,18 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           tc::tmem_wait_ld();
           const int64_t col0 = n0 + ch * 32;
           if (!row_ok || col0 >= p.N) continue;
+          if (p.partial) {  // split-K partial tile, fp32 [split][M][N]
+            float* prow = p.partial + ((int64_t)(t / total_tiles) * p.M + row) * p.N + col0;
+            if (col0 + 32 <= p.N && (p.N & 3) == 0) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                reinterpret_cast<float4*>(prow)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            } else {
+              for (int j = 0; j < 32 && col0 + j < p.N; ++j) prow[j] = __uint_as_float(r[j]);
+            }
+            continue;
+          }
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
@@ -367,11 +393,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     uint32_t phase = 0;
     constexpr int FIPT = (BN * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
     float fsc[FIPT];
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      int m0, n0, b;
+    for (int t = blockIdx.x; t < total_work; t += gridDim.x) {
+      int m0, n0, b, kb0, kb1;
       tile_coords(t, m0, n0, b);
+      k_range(t, kb0, kb1);
       bool ok = true;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc::mbar_wait(&full[stage], phase, p.err) || *abort_flag) {
           ok = false;
           break;
@@ -382,7 +409,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
           // block-64 scales change with the K block; per-row scales were loaded once for the tile
-          if (p.scale_layout == 0 || kb == 0) {
+          if (p.scale_layout == 0 || kb == kb0) {
 #pragma unroll
             for (int u = 0; u < FIPT; ++u) {  // every scale load in flight before the first is used
               const int i = dt + u * NDQ;
@@ -475,11 +502,40 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& 
       return rc;
     attr_set = true;
   }
-  int tiles = p.m_tiles * p.n_tiles * (int)p.batch;
+  int tiles = p.m_tiles * p.n_tiles * (int)p.batch * p.ksplit;
   int grid = std::min(tiles, device_info().sm_count);
   LaunchScope ls(name, st);
   gemm_tc_kernel<BN, BF16, DEQ, MSUB><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
   return after_launch(name);
+}
+
+// C = alpha * sum_s partial[s] + beta * bias, converted to the output type with C's strides.
+template <typename OutT>
+__global__ void __launch_bounds__(256) gemm_splitk_reduce(const float* __restrict__ part, int ksplit, int64_t M,
+                                                          int64_t N, OutT* __restrict__ c, int64_t c_sm, int64_t c_sn,
+                                                          const OutT* __restrict__ bias, int64_t bias_sm,
+                                                          int64_t bias_sn, float alpha, float beta) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < ksplit; ++s) acc += part[(int64_t)s * total + i];
+    const int64_t m = i / N, n = i % N;
+    float v = alpha * acc;
+    if (bias) v += beta * to_f32(bias[m * bias_sm + n * bias_sn]);
+    c[m * c_sm + n * c_sn] = from_f32<OutT>(v);
+  }
+}
+
+// Split-K plan: GEMMs with too few output tiles to fill the GPU but a long reduction (the LoRA
+// projections: N or M = 16, K = 2048..4096) give each SM a slice of K instead.
+void splitk_plan(int64_t tiles, int k_blocks, int& ksplit, int& kps) {
+  const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
+  ksplit = 1, kps = k_blocks;
+  if (tiles * 2 > sms || k_blocks < 8) return;
+  int want = (int)std::min<int64_t>(sms / tiles, k_blocks / 4);  // at least 4 K blocks per slice
+  if (want < 2) return;
+  kps = (k_blocks + want - 1) / want;
+  ksplit = (k_blocks + kps - 1) / kps;
 }
 
 // Wave-quantisation aware choice between 128- and 256-wide tiles.
@@ -538,6 +594,14 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
   p.bias_sb = a->bias_sb, p.bias_sm = a->bias_sm, p.bias_sn = a->bias_sn;
   p.alpha = a->alpha, p.beta = a->beta;
   p.err = device_error_ptr();
+  p.ksplit = 1, p.kps = p.k_blocks;
+  if (a->batch == 1 && a->workspace) {
+    int ks, kps;
+    splitk_plan((int64_t)p.m_tiles * p.n_tiles, p.k_blocks, ks, kps);
+    if (ks > 1 && (uint64_t)a->workspace_bytes >= (uint64_t)ks * a->M * a->N * sizeof(float) &&
+        ((uintptr_t)a->workspace & 15) == 0)
+      p.ksplit = ks, p.kps = kps, p.partial = (float*)a->workspace;
+  }
 
   CUtensorMap ta, tb;
   {
@@ -572,11 +636,34 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
     if (!make_tmap(&tb, dt, rank, a->b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return fail(B2_ERR_ARG, "gemm_tc: tensor map for B rejected");
   }
+  int rc;
   if (BN == 256)
-    return bf16 ? launch_kernel<256, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn256")
-                : launch_kernel<256, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn256");
-  return bf16 ? launch_kernel<128, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn128")
+    rc = bf16 ? launch_kernel<256, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn256")
+              : launch_kernel<256, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn256");
+  else
+    rc = bf16 ? launch_kernel<128, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn128")
               : launch_kernel<128, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn128");
+  if (rc || p.ksplit == 1) return rc;
+  const int64_t total = a->M * a->N;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)device_info().sm_count * 8);
+  LaunchScope ls("gemm_splitk_reduce", st);
+  const void* bias = p.has_bias ? a->bias : nullptr;
+  if (bf16)
+    gemm_splitk_reduce<__nv_bfloat16><<<grid, 256, 0, st>>>(p.partial, p.ksplit, a->M, a->N, (__nv_bfloat16*)a->c, a->c_sm,
+                                                            a->c_sn, (const __nv_bfloat16*)bias, a->bias_sm, a->bias_sn,
+                                                            a->alpha, a->beta);
+  else
+    gemm_splitk_reduce<__half><<<grid, 256, 0, st>>>(p.partial, p.ksplit, a->M, a->N, (__half*)a->c, a->c_sm, a->c_sn,
+                                                     (const __half*)bias, a->bias_sm, a->bias_sn, a->alpha, a->beta);
+  return after_launch("gemm_splitk_reduce");
+}
+
+uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a) {
+  if (a->batch != 1 || a->K == 0 || !gemm_tc_eligible(a)) return 0;
+  const int BN = pick_bn(a->M, a->N, a->batch);
+  int ks, kps;
+  splitk_plan(((a->M + BM - 1) / BM) * ((a->N + BN - 1) / BN), (int)((a->K + BK - 1) / BK), ks, kps);
+  return ks > 1 ? (uint64_t)ks * a->M * a->N * sizeof(float) : 0;
 }
 
 }  // namespace b2
@@ -629,6 +716,7 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   p.alpha = 1.f, p.beta = 1.f;
   p.err = device_error_ptr();
   p.scale = a->scale, p.scale_layout = a->scale_layout, p.scale_nb = (a->K + 63) / 64, p.deq_rows = a->N;
+  p.ksplit = 1, p.kps = p.k_blocks;
   CUtensorMap ta, tb;
   {
     uint64_t dims[2] = {(uint64_t)red, (uint64_t)a->M}, strides[1] = {(uint64_t)a->x_ld * 2};

@@ -142,6 +142,12 @@ at::Tensor run_gemm(const at::Tensor& a, const at::Tensor& b, const at::Tensor* 
     count(name);
     return out;
   }
+  // split-K scratch (few output tiles, long K: the LoRA projections) from the caching allocator
+  at::Tensor ws;
+  if (const uint64_t wsb = b2_gemm_workspace_bytes(&g)) {
+    ws = at::empty({(int64_t)wsb}, a.options().dtype(at::kByte));
+    g.workspace = ws.data_ptr(), g.workspace_bytes = (int64_t)wsb;
+  }
   b2_check(b2_gemm(&g, cur_stream()), name);
   count(name);
   return out;
@@ -669,6 +675,40 @@ at::Tensor b2_int8_linear_dx(const at::Tensor& dy0, const at::Tensor& q, const a
   return dx.view(osz);
 }
 
+// One AdamW step for a list of parameters (the arithmetic and roundings of torch.optim.AdamW with
+// foreach=False, csrc/ops_ew.cpp:432-451), one launch per 48 tensors instead of ~6 per tensor.
+void b2_adamw_step_op(at::TensorList params, at::TensorList grads, at::TensorList exp_avgs, at::TensorList exp_avg_sqs,
+                      double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step) {
+  const size_t n = params.size();
+  TORCH_CHECK(grads.size() == n && exp_avgs.size() == n && exp_avg_sqs.size() == n, "adamw_step_: list lengths differ");
+  TORCH_CHECK(step >= 1, "adamw_step_: step must be >= 1");
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(params[0].device());
+  const auto dt = params[0].scalar_type();
+  TORCH_CHECK(dt == at::kFloat || dt == at::kBFloat16, "adamw_step_: parameters must be float32 or bfloat16");
+  std::vector<void*> P(n), M(n), V(n);
+  std::vector<const void*> G(n);
+  std::vector<int64_t> N(n);
+  for (size_t i = 0; i < n; ++i) {
+    for (const at::Tensor* t : {&params[i], &grads[i], &exp_avgs[i], &exp_avg_sqs[i]}) {
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == dt && t->is_contiguous() && t->device() == params[0].device(),
+                  "adamw_step_: every tensor must be a contiguous CUDA tensor of the parameters' dtype and device");
+      TORCH_CHECK(t->numel() == params[i].numel(), "adamw_step_: shape mismatch");
+    }
+    P[i] = params[i].data_ptr(), G[i] = grads[i].data_ptr(), M[i] = exp_avgs[i].data_ptr(), V[i] = exp_avg_sqs[i].data_ptr();
+    N[i] = params[i].numel();
+  }
+  b2_adamw_args a{};
+  a.param = P.data(), a.grad = G.data(), a.exp_avg = M.data(), a.exp_avg_sq = V.data(), a.numel = N.data();
+  a.n = (int32_t)n;
+  a.dtype = dt == at::kFloat ? B2_F32 : B2_BF16;
+  a.lr = (float)lr, a.beta1 = (float)beta1, a.beta2 = (float)beta2, a.eps = (float)eps, a.weight_decay = (float)weight_decay;
+  a.bias_correction1 = (float)(1.0 - std::pow(beta1, (double)step));
+  a.bias_correction2 = (float)(1.0 - std::pow(beta2, (double)step));
+  b2_check(b2_adamw_step(&a, cur_stream()), "adamw_step_");
+  count("b2::adamw_step_");
+}
+
 // =============================== registration ======================================================
 
 std::mutex g_reg_mu;
@@ -739,6 +779,8 @@ TORCH_LIBRARY(b2, m) {
   m.def("dequant_int8(Tensor q, Tensor scale, ScalarType out_dtype) -> Tensor");
   m.def("int8_linear_fwd(Tensor x, Tensor q, Tensor scale, Tensor? bias) -> Tensor");
   m.def("int8_linear_dx(Tensor dy, Tensor q, Tensor scale) -> Tensor");
+  m.def("adamw_step_(Tensor(a!)[] params, Tensor[] grads, Tensor(b!)[] exp_avgs, Tensor(c!)[] exp_avg_sqs, float lr, "
+        "float beta1, float beta2, float eps, float weight_decay, int step) -> ()");
   m.def("set_enabled(bool on) -> ()", &op_set_enabled);
   m.def("is_enabled() -> bool", &op_is_enabled);
   m.def("set_fused_attention(int mode) -> ()", &op_set_fused_attention);
@@ -751,4 +793,5 @@ TORCH_LIBRARY_IMPL(b2, CUDA, m) {
   m.impl("dequant_int8", &b2_dequant_int8_op);
   m.impl("int8_linear_fwd", &b2_int8_linear_fwd);
   m.impl("int8_linear_dx", &b2_int8_linear_dx);
+  m.impl("adamw_step_", &b2_adamw_step_op);
 }

@@ -127,24 +127,30 @@ def block_flops(tokens=1024, text_tokens=512, hidden=2048, text_dim=1024, mlp=81
     return lin_f + attn_f, lin_b + 2.5 * attn_f
 
 
-def make_optimizer(params, lr=1e-4):
-    """AdamW(foreach=False): the per-tensor addcmul_/addcdiv_/lerp_ path the reference's trainer uses."""
+def make_optimizer(params, lr=1e-4, fused=False):
+    """AdamW(foreach=False): the per-tensor addcmul_/addcdiv_/lerp_ path the reference's trainer uses;
+    fused=True: the same arithmetic as one multi-tensor launch per 48 parameters (FusedAdamW)."""
+    if fused:
+        from torch_vulkan_b200.optim import FusedAdamW
+
+        return FusedAdamW(params, lr=lr, betas=(0.9, 0.999), weight_decay=0.01)
     return torch.optim.AdamW(params, lr=lr, betas=(0.9, 0.999), weight_decay=0.01, foreach=False)
 
 
 class LoRATrainer:
     """One LoRA training step of a DiTStack: forward, MSE loss against the target, backward, data-parallel
     gradient averaging (bucketed per block, overlapped with the backward when torch.distributed is
-    initialised), AdamW(foreach=False) on the LoRA parameters."""
+    initialised), AdamW on the LoRA parameters (per-tensor foreach=False ops, or fused_optimizer=True for
+    the multi-tensor kernel)."""
 
-    def __init__(self, model: DiTStack, lr=1e-4):
+    def __init__(self, model: DiTStack, lr=1e-4, fused_optimizer=False):
         from torch_vulkan_b200.dp import BucketedGradAllReduce
 
         self.model = model
         buckets = [[p for n, p in b.named_parameters() if "lora_" in n] for b in model.blocks]
         self.params = [p for bk in buckets for p in bk]
         self.reducer = BucketedGradAllReduce(buckets)
-        self.opt = make_optimizer(self.params, lr=lr)
+        self.opt = make_optimizer(self.params, lr=lr, fused=fused_optimizer)
 
     def step(self, x, text, cond, target):
         out = self.model(x, text, cond)
