@@ -18,6 +18,8 @@
 // drains its own TMA copies (bounded) and frees TMEM before returning.
 #include <cuda.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <type_traits>
 
@@ -98,17 +100,25 @@ struct Cfg {
   static constexpr int A_BYTES = BMT * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int R_BYTES = DEQ ? BN * BK : 0;  // raw int8 tile
-  static constexpr int STAGE = A_BYTES + B_BYTES + R_BYTES;
-  static constexpr int STAGES = (196 * 1024) / STAGE > 8 ? 8 : (196 * 1024) / STAGE;
+  // bf16: a TMA stage holds A and B. int8: a TMA stage holds A and the raw int8 tile; the dequantised
+  // bf16 B tiles live in their own NB-deep ring, so the TMA ring (which must cover the load latency)
+  // is not sized by the dequant buffers.
+  static constexpr int STAGE = A_BYTES + (DEQ ? R_BYTES : B_BYTES);
+  static constexpr int NB = DEQ ? 2 : 0;
+  static constexpr int BUDGET = 224 * 1024 - NB * B_BYTES;
+  static constexpr int STAGES = BUDGET / STAGE > 8 ? 8 : BUDGET / STAGE;
+  static constexpr int OFF_B = STAGES * STAGE;  // int8: the B ring
   // int8 dequant warps run pure ALU work; they take warp ids 6-8, 10-12, 14-15 so that none shares
   // a scheduler (warp id % 4) with the MMA-issuing warp 1, whose issue slots they would otherwise
   // take (warps 9 and 13 idle).
   static constexpr int DEQ_WARPS = DEQ ? 8 : 0;
   static constexpr int THREADS = DEQ ? 16 * 32 : 6 * 32;
-  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  static constexpr int SMEM = OFF_B + NB * B_BYTES + 1024 + 256;
+  static_assert(SMEM <= 232448, "GEMM stages exceed the 227 KB shared-memory limit");
   static constexpr uint32_t SUB_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per M sub-tile
   static constexpr uint32_t ACC_COLS = MSUB * SUB_COLS;  // one accumulator (all M sub-tiles)
-  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;    // double-buffered (a power of two)
+  static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;  // double-buffered when it fits
+  static constexpr uint32_t TMEM_COLS = NACC * ACC_COLS;   // (a power of two)
   static_assert(TMEM_COLS <= 512, "accumulators exceed TMEM");
   static_assert(BN % 16 == 0 && BN <= 256, "UMMA N must be a multiple of 16 up to 256");
 };
@@ -155,13 +165,16 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
   constexpr int NDQ = C::DEQ_WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::STAGE);
+  constexpr int NB = C::NB > 0 ? C::NB : 1;
+  constexpr int NACC = C::NACC;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_B + C::NB * C::B_BYTES);
   uint64_t* full = bars;                // [S]  TMA landed
   uint64_t* empty = bars + S;           // [S]  MMA done reading the stage
   uint64_t* tfull = bars + 2 * S;       // [2]  accumulator ready
   uint64_t* tempty = bars + 2 * S + 2;  // [2]  accumulator drained
-  uint64_t* bready = bars + 2 * S + 4;  // [S]  (int8) B stage dequantised
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+  uint64_t* bready = bars + 2 * S + 4;       // [NB] (int8) B buffer dequantised
+  uint64_t* bfree = bars + 2 * S + 4 + NB;   // [NB] (int8) MMAs reading the B buffer done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4 + 2 * NB);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -172,7 +185,10 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     for (int i = 0; i < S; ++i) {
       tc::mbar_init(&full[i], 1);
       tc::mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < NB; ++i) {
       tc::mbar_init(&bready[i], NDQ > 0 ? NDQ : 1);
+      tc::mbar_init(&bfree[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&tfull[i], 1);
@@ -225,8 +241,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
           uint8_t* sa = smem + stage * C::STAGE;
           uint8_t* sb = sa + C::A_BYTES;
-          uint8_t* sr = sb + C::B_BYTES;
-          const uint32_t bytes = C::A_BYTES + (DEQ ? C::R_BYTES : C::B_BYTES);
+          uint8_t* sr = sa + C::A_BYTES;  // int8: the raw tile follows A
+          const uint32_t bytes = C::STAGE;
           tc::mbar_arrive_expect_tx(&full[stage], bytes);
           const int k0 = kb * BK;
           if (!p.a_mn) {  // one box of BMT rows x 64 k
@@ -279,25 +295,28 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
+      int gk = 0;  // K blocks consumed so far (B ring position)
       bool ok = true;
       for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x, ++it) {
         int kb0, kb1;
         k_range(t, kb0, kb1);
-        const int acc = it & 1;
-        if (!tc::mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, p.err) || *abort_flag) {
+        const int acc = it % NACC;
+        if (!tc::mbar_wait(&tempty[acc], ((it / NACC) & 1) ^ 1, p.err) || *abort_flag) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
         const uint32_t d = tbase + (uint32_t)(acc * C::ACC_COLS);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!tc::mbar_wait(&full[stage], phase, p.err) || (DEQ && !tc::mbar_wait(&bready[stage], phase, p.err))) {
+          const int bb = gk % NB;
+          if (!tc::mbar_wait(&full[stage], phase, p.err) ||
+              (DEQ && !tc::mbar_wait(&bready[bb], (uint32_t)((gk / NB) & 1), p.err))) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
           uint8_t* sa = smem + stage * C::STAGE;
-          uint8_t* sb = sa + C::A_BYTES;
+          uint8_t* sb = DEQ ? smem + C::OFF_B + bb * C::B_BYTES : sa + C::A_BYTES;
           const tc::SDesc ad0 = tc::sdesc_parts(tc::smem_u32(sa), a_lbo, 1024);
           const tc::SDesc bd0 = tc::sdesc_parts(tc::smem_u32(sb), b_lbo, 1024);
           const uint32_t acc0 = kb > kb0 ? 1u : 0u;
@@ -310,6 +329,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
                              k > 0 ? 1u : acc0);
           }
           tc::mma_commit(&empty[stage]);
+          if (DEQ) tc::mma_commit(&bfree[bb]);
+          ++gk;
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -326,8 +347,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     int it = 0;
     using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     for (int t = blockIdx.x; t < total_work; t += gridDim.x, ++it) {
-      const int acc = it & 1;
-      if (!tc::mbar_wait(&tfull[acc], (it >> 1) & 1, p.err) || *abort_flag) {
+      const int acc = it % NACC;
+      if (!tc::mbar_wait(&tfull[acc], (it / NACC) & 1, p.err) || *abort_flag) {
         *abort_flag = 1;
         break;
       }
@@ -391,6 +412,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
     int stage = 0;
     uint32_t phase = 0;
+    int gk = 0;  // K blocks dequantised so far (B ring position)
     constexpr int FIPT = (BN * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
     float fsc[FIPT];
     for (int t = blockIdx.x; t < total_work; t += gridDim.x) {
@@ -403,8 +425,13 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           ok = false;
           break;
         }
-        uint8_t* sb = smem + stage * C::STAGE + C::A_BYTES;
-        const uint8_t* sr = sb + C::B_BYTES;
+        const int bb = gk % NB;
+        if (!tc::mbar_wait(&bfree[bb], (uint32_t)(((gk / NB) & 1) ^ 1), p.err)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sb = smem + C::OFF_B + bb * C::B_BYTES;
+        const uint8_t* sr = smem + stage * C::STAGE + C::A_BYTES;
         if (!p.b_mn) {
           // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
@@ -468,7 +495,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
         }
         tc::fence_async_shared();
-        tc::mbar_arrive(&bready[stage]);
+        tc::mbar_arrive(&bready[bb]);
+        ++gk;
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
@@ -690,19 +718,26 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   // tiles (256 rows) halve it; among the shapes the kernel supports, take the one with the best
   // wave-quantised SM utilisation, weighted by how well the dequant warps keep up.
   struct Choice { int bn, msub; double eff; };
-  const Choice fwd_opts[] = {{128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
-  const Choice dx_opts[] = {{128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const Choice fwd_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const Choice dx_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
   const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
   Choice best{0, 0, -1.0};
   double best_score = -1.0;
-  const int nopts = a->transpose_w ? 3 : 4;
+  const int nopts = a->transpose_w ? 4 : 5;
+  static const int forced = [] {  // B2_INT8_TILE=<bn>x<msub> pins the tile (measurement sweeps)
+    const char* e = getenv("B2_INT8_TILE");
+    int bn = 0, ms = 0;
+    return (e && sscanf(e, "%dx%d", &bn, &ms) == 2) ? bn * 10 + ms : 0;
+  }();
   for (int i = 0; i < nopts; ++i) {
     const Choice c = a->transpose_w ? dx_opts[i] : fwd_opts[i];
     const int64_t tiles = ((a->M + 128 * c.msub - 1) / (128 * c.msub)) * ((out_cols + c.bn - 1) / c.bn);
     const int64_t waves = (tiles + sms - 1) / sms;
-    const double score = (double)a->M * out_cols / ((double)waves * sms * 128 * c.msub * c.bn) * c.eff;
+    double score = (double)a->M * out_cols / ((double)waves * sms * 128 * c.msub * c.bn) * c.eff;
+    if (forced) score = (forced == c.bn * 10 + c.msub) ? 1e9 : -1.0;
     if (score > best_score) best_score = score, best = c;
   }
+  if (best.bn == 0) best = a->transpose_w ? dx_opts[1] : fwd_opts[1];
   const int BN = best.bn, BMT = 128 * best.msub;
   TcParams p{};
   p.M = a->M, p.N = out_cols, p.K = red, p.batch = 1;
@@ -733,6 +768,7 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
       return fail(B2_ERR_ARG, "int8_gemm: tensor map for q rejected");
   }
   const char* name = a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd";
+  if (best.msub == 2 && BN == 256) return launch_kernel<256, true, 1, 2>(ta, tb, p, st, name);
   if (best.msub == 2 && BN == 128) return launch_kernel<128, true, 1, 2>(ta, tb, p, st, name);
   if (best.msub == 2 && BN == 96) return launch_kernel<96, true, 1, 2>(ta, tb, p, st, name);
   if (BN == 256) return launch_kernel<256, true, 1, 1>(ta, tb, p, st, name);
