@@ -566,18 +566,33 @@ void splitk_plan(int64_t tiles, int k_blocks, int& ksplit, int& kps) {
   ksplit = (k_blocks + kps - 1) / kps;
 }
 
-// Wave-quantisation aware choice between 128- and 256-wide tiles.
-int pick_bn(int64_t M, int64_t N, int64_t batch) {
+// Wave-quantisation aware choice among 128x128, 128x256 and 256x256 CTA tiles, each weighted by its
+// measured per-SM rate (wider tiles need less operand bandwidth per FLOP).
+struct TileChoice {
+  int bn, msub;
+};
+TileChoice pick_tile(int64_t M, int64_t N, int64_t batch) {
   const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
-  auto score = [&](int bn, double tile_eff) {
-    int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn) * batch;
-    int64_t waves = (tiles + sms - 1) / sms;
-    double useful = (double)M * N * batch;
-    double work = (double)waves * sms * BM * bn;
-    return useful / work * tile_eff;
+  static const int forced = [] {  // B2_GEMM_TILE=<bn>x<msub> pins the tile (measurement sweeps)
+    const char* e = getenv("B2_GEMM_TILE");
+    int bn = 0, ms = 0;
+    return (e && sscanf(e, "%dx%d", &bn, &ms) == 2) ? bn * 10 + ms : 0;
+  }();
+  struct Opt {
+    int bn, msub;
+    double eff;
   };
-  // 128-wide tiles need 1.5x the operand bandwidth per FLOP of 256-wide ones (measured: ~0.65x the rate)
-  return score(256, 1.0) >= score(128, 0.65) ? 256 : 128;
+  const Opt opts[] = {{256, 2, 1.1}, {256, 1, 1.0}, {128, 1, 0.65}};
+  TileChoice best{256, 1};
+  double best_score = -1.0;
+  for (const Opt& o : opts) {
+    const int64_t tiles = ((M + BM * o.msub - 1) / (BM * o.msub)) * ((N + o.bn - 1) / o.bn) * batch;
+    const int64_t waves = (tiles + sms - 1) / sms;
+    double score = (double)M * N * batch / ((double)waves * sms * BM * o.msub * o.bn) * o.eff;
+    if (forced) score = forced == o.bn * 10 + o.msub ? 1e9 : -1.0;
+    if (score > best_score) best_score = score, best = TileChoice{o.bn, o.msub};
+  }
+  return best;
 }
 
 }  // namespace
@@ -607,10 +622,11 @@ bool gemm_tc_eligible(const b2_gemm_args* a) {
 int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
   const bool bf16 = a->dtype == B2_BF16;
   const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const int BN = pick_bn(a->M, a->N, a->batch);
+  const TileChoice tc_ = pick_tile(a->M, a->N, a->batch);
+  const int BN = tc_.bn, BMT = BM * tc_.msub;
   TcParams p{};
   p.M = a->M, p.N = a->N, p.K = a->K, p.batch = a->batch;
-  p.m_tiles = (int)((a->M + BM - 1) / BM);
+  p.m_tiles = (int)((a->M + BMT - 1) / BMT);
   p.n_tiles = (int)((a->N + BN - 1) / BN);
   p.k_blocks = (int)((a->K + BK - 1) / BK);
   p.a_mn = !(a->a_sk == 1 && (a->M == 1 || tma_ok_stride(a->a_sm, 2)));
@@ -638,7 +654,7 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
     int rank = p.a3d ? 3 : 2;
     if (!p.a_mn) {
       dims[0] = a->K, dims[1] = a->M, strides[0] = (uint64_t)(a->M == 1 ? a->K : a->a_sm) * 2;
-      box[0] = 64, box[1] = BM;
+      box[0] = 64, box[1] = (uint32_t)BMT;
     } else {
       dims[0] = a->M, dims[1] = a->K, strides[0] = (uint64_t)(a->K == 1 ? a->M : a->a_sk) * 2;
       box[0] = 64, box[1] = 64;
@@ -665,7 +681,10 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
       return fail(B2_ERR_ARG, "gemm_tc: tensor map for B rejected");
   }
   int rc;
-  if (BN == 256)
+  if (BN == 256 && tc_.msub == 2)
+    rc = bf16 ? launch_kernel<256, true, 0, 2>(ta, tb, p, st, "gemm_tc_256x256")
+              : launch_kernel<256, false, 0, 2>(ta, tb, p, st, "gemm_tc_256x256");
+  else if (BN == 256)
     rc = bf16 ? launch_kernel<256, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn256")
               : launch_kernel<256, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn256");
   else
@@ -688,9 +707,10 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
 
 uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a) {
   if (a->batch != 1 || a->K == 0 || !gemm_tc_eligible(a)) return 0;
-  const int BN = pick_bn(a->M, a->N, a->batch);
+  const TileChoice t = pick_tile(a->M, a->N, a->batch);
+  const int64_t BMT = BM * t.msub;
   int ks, kps;
-  splitk_plan(((a->M + BM - 1) / BM) * ((a->N + BN - 1) / BN), (int)((a->K + BK - 1) / BK), ks, kps);
+  splitk_plan(((a->M + BMT - 1) / BMT) * ((a->N + t.bn - 1) / t.bn), (int)((a->K + BK - 1) / BK), ks, kps);
   return ks > 1 ? (uint64_t)ks * a->M * a->N * sizeof(float) : 0;
 }
 
