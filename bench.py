@@ -567,6 +567,14 @@ def run_case(name, iters):
 
 
 def main():
+    # Exactly one JSON line goes to stdout: everything else that writes to file descriptor 1 during
+    # the run (NCCL's version banner, library prints) is sent to stderr.
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    _main(json_out)
+
+
+def _main(json_out):
     args = parse()
     if args.case:
         run_case(args.case, args.case_iters)
@@ -577,7 +585,7 @@ def main():
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=json_out, flush=True)
         return
     if world > 1:
         import datetime
@@ -591,7 +599,7 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=json_out, flush=True)
 
 
 if __name__ == "__main__":
