@@ -787,6 +787,12 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __rest
   tc::pdl_trigger();
   const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
   const int64_t q0 = (int64_t)blockIdx.x * 64;
+  if (blockIdx.z == 1) {  // the zeroing blocks run beside the delta blocks
+    float4* acc = reinterpret_cast<float4*>(dq_acc + (bh * (sq_pad / 64) + blockIdx.x) * (128 * 64));
+#pragma unroll
+    for (int it = 0; it < 8; ++it) acc[threadIdx.x + it * 256] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
   // thread = (row, quarter of the 128-wide row): 4 x 16-byte loads of O and of dO, all in flight at once
   const int row = threadIdx.x >> 2, qtr = threadIdx.x & 3;
   const int64_t q = q0 + row;
@@ -812,9 +818,6 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __rest
   s += __shfl_xor_sync(0xffffffffu, s, 2);
   if (qtr == 0)
     lsed[bh * sq_pad + q] = q < Sq ? make_float2(lse[bh * Sq + q] * 1.4426950408889634f, s) : make_float2(INFINITY, 0.f);
-  float4* acc = reinterpret_cast<float4*>(dq_acc + (bh * (sq_pad / 64) + blockIdx.x) * (128 * 64));
-#pragma unroll
-  for (int it = 0; it < 8; ++it) acc[threadIdx.x + it * 256] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dq[b,h,q,:] = bf16(dq_acc[bh][:][q]), one block per (64-query tile, batch*head), transposed through
@@ -822,23 +825,24 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __rest
 __global__ void __launch_bounds__(256) attn_dq_convert(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dq,
                                                        int64_t H, int64_t Sq, int64_t sq_pad, int64_t s0, int64_t s1,
                                                        int64_t s2, float scale) {
-  __shared__ float t[128][65];
+  __shared__ float t[128][33];
   tc::pdl_wait();
   tc::pdl_trigger();
   const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
-  const int64_t q0 = (int64_t)blockIdx.x * 64;
-  const float4* src = reinterpret_cast<const float4*>(dq_acc + (bh * (sq_pad / 64) + blockIdx.x) * (128 * 64));
+  const int half = blockIdx.x & 1;
+  const int64_t q0 = (int64_t)(blockIdx.x >> 1) * 64 + half * 32;
+  const float* tile = dq_acc + (bh * (sq_pad / 64) + (blockIdx.x >> 1)) * (128 * 64) + half * 32;
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int e = threadIdx.x + it * 256;
-    const int d = e >> 4, j = (e & 15) * 4;
-    float4 v = src[e];
+  for (int it = 0; it < 4; ++it) {
+    const int e = threadIdx.x + it * 256;  // 128 d-rows x 8 float4
+    const int d = e >> 3, j = (e & 7) * 4;
+    float4 v = *reinterpret_cast<const float4*>(tile + d * 64 + j);
     t[d][j] = v.x * scale, t[d][j + 1] = v.y * scale, t[d][j + 2] = v.z * scale, t[d][j + 3] = v.w * scale;
   }
   __syncthreads();
 #pragma unroll
-  for (int it = 0; it < 4; ++it) {
-    const int e = threadIdx.x + it * 256;  // 64 rows x 16 chunks of 8 d
+  for (int it = 0; it < 2; ++it) {
+    const int e = threadIdx.x + it * 256;  // 32 rows x 16 chunks of 8 d
     const int j = e >> 4, d0 = (e & 15) * 8;
     const int64_t q = q0 + j;
     if (q >= Sq) continue;
@@ -886,7 +890,7 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   float* dq_acc = (float*)a->workspace;
   float2* lsed = reinterpret_cast<float2*>(dq_acc + a->B * a->H * a->D * sq_pad);
   {
-    dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
+    dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H), 2);
     if (int rc = launch_pdl("attn_bwd_prep", attn_bwd_prep, grid, dim3(256), 0, st, (const __nv_bfloat16*)a->o,
                             (const __nv_bfloat16*)a->d_o, (const float*)a->lse, lsed, dq_acc, (int64_t)a->H,
                             (int64_t)a->Sq, sq_pad, a->o_s[0], a->o_s[1], a->o_s[2], a->do_s[0], a->do_s[1],
@@ -923,7 +927,7 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
       return rc;
   }
   if (a->dq) {
-    dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H));
+    dim3 grid((unsigned)(sq_pad / 32), (unsigned)(a->B * a->H));
     if (int rc = launch_pdl("attn_dq_convert", attn_dq_convert, grid, dim3(256), 0, st, (const float*)dq_acc,
                             (__nv_bfloat16*)a->dq, (int64_t)a->H, (int64_t)a->Sq, sq_pad, a->dq_s[0], a->dq_s[1],
                             a->dq_s[2], a->scale))
