@@ -105,3 +105,13 @@ def test_fused_adamw_matches_foreach_false(tv, dt):
     tol = 1e-6 if dt == torch.float32 else 1e-2
     for a, b in zip(got, ref):
         assert torch.allclose(a, b, rtol=tol, atol=tol), (a - b).abs().max()
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_addcmul_broadcast_row(tv, dt):
+    """x + g * y with g one broadcast row (the DiT residual update): the [rows, C] vectorised path."""
+    x = rnd_range((2, 96, 256), dt, seed=31)
+    g = rnd_range((1, 1, 256), dt, seed=32)
+    y = rnd_range((2, 96, 256), dt, seed=33)
+    ew_close(torch.addcmul(x.cuda(), g.cuda(), y.cuda()), oracle.addcmul(x, g, y, 1.0), dt, scale=2.0)
+    ew_close(torch.addcmul(x.cuda(), y.cuda(), g.cuda(), value=0.5), oracle.addcmul(x, y, g, 0.5), dt, scale=2.0)

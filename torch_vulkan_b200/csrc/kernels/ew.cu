@@ -59,6 +59,43 @@ __global__ void ew_contig(T* __restrict__ out, const T* x, const T* __restrict__
     out[i] = from_f32<T>(ternary(op, to_f32(x[i]), to_f32(t1[i]), op != 2 ? to_f32(t2[i]) : 0.f, v));
 }
 
+// [rows, C] operands whose rows are either contiguous (row stride C) or one broadcast row (row
+// stride 0), C contiguous: the residual update x + g * branch with g a per-channel vector.
+template <typename T, int V>
+__global__ void ew_rows(T* __restrict__ out, const T* x, const T* __restrict__ t1, const T* __restrict__ t2,
+                        int64_t rows, int64_t C, int64_t xs, int64_t s1, int64_t s2, int op, float v) {
+  const int64_t cv = C / V, nv = rows * cv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cv, c = (i - r * cv) * V;
+    T xv[V], av[V], bv[V], ov[V];
+    *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(x + r * xs + c);
+    *reinterpret_cast<uint4*>(av) = *reinterpret_cast<const uint4*>(t1 + r * s1 + c);
+    if (op != 2) *reinterpret_cast<uint4*>(bv) = *reinterpret_cast<const uint4*>(t2 + r * s2 + c);
+#pragma unroll
+    for (int k = 0; k < V; ++k)
+      ov[k] = from_f32<T>(ternary(op, to_f32(xv[k]), to_f32(av[k]), op != 2 ? to_f32(bv[k]) : 0.f, v));
+    *reinterpret_cast<uint4*>(out + r * C + c) = *reinterpret_cast<uint4*>(ov);
+  }
+}
+
+// Row stride of an operand that is either contiguous over `sizes` or one broadcast row: C or 0;
+// -1 otherwise.
+int64_t row_stride(const b2_ew_args* a, const int64_t* s) {
+  const int nd = a->ndim;
+  const int64_t C = a->sizes[nd - 1];
+  if (C > 1 && s[nd - 1] != 1) return -1;
+  bool contig = true, bcast = true;
+  int64_t expect = C;
+  for (int d = nd - 2; d >= 0; --d) {
+    if (a->sizes[d] != 1) {
+      if (s[d] != expect) contig = false;
+      if (s[d] != 0) bcast = false;
+    }
+    expect *= a->sizes[d];
+  }
+  return contig ? C : bcast ? 0 : -1;
+}
+
 template <typename T>
 int ew_run(const b2_ew_args* a, cudaStream_t st) {
   int64_t n = 1;
@@ -77,9 +114,18 @@ int ew_run(const b2_ew_args* a, cudaStream_t st) {
   constexpr int V = 16 / sizeof(T);
   bool al = ((uintptr_t)a->out | (uintptr_t)a->x | (uintptr_t)a->t1 | (a->op != 2 ? (uintptr_t)a->t2 : 0)) % 16 == 0;
   LaunchScope ls(a->op == 0 ? "ew_addcmul" : a->op == 1 ? "ew_addcdiv" : "ew_lerp", st);
+  const int64_t C = a->ndim > 0 ? a->sizes[a->ndim - 1] : 1;
+  const int64_t rs_out = a->ndim > 0 ? row_stride(a, a->out_s) : -1, rs_x = a->ndim > 0 ? row_stride(a, a->x_s) : -1;
+  const int64_t rs1 = a->ndim > 0 ? row_stride(a, a->t1_s) : -1;
+  const int64_t rs2 = (a->ndim > 0 && a->op != 2) ? row_stride(a, a->t2_s) : 0;
   if (contig && al) {
     int grid = grid_for(n / V + 1, 256, 8);
     ew_contig<T, V><<<grid, 256, 0, st>>>((T*)a->out, (const T*)a->x, (const T*)a->t1, (const T*)a->t2, n, a->op, a->value);
+  } else if (al && C % V == 0 && rs_out == C && rs_x >= 0 && rs1 >= 0 && rs2 >= 0) {
+    const int64_t rows = n / C;
+    int grid = grid_for(n / V, 256, 8);
+    ew_rows<T, V><<<grid, 256, 0, st>>>((T*)a->out, (const T*)a->x, (const T*)a->t1, (const T*)a->t2, rows, C, rs_x, rs1,
+                                        rs2, a->op, a->value);
   } else {
     Strides8 s{};
     s.ndim = a->ndim;

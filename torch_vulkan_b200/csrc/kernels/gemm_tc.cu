@@ -385,9 +385,21 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
           if (p.has_bias) {
+            const OutT* bp = brow + col0 * p.bias_sn;
+            if (p.bias_sn == 1 && col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {
+              // a contiguous bias row segment (addmm with a full-matrix or broadcast-row bias): 4 x 16 B
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.N) v[j] += p.beta * to_f32(brow[(col0 + j) * p.bias_sn]);
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const uint4 raw = reinterpret_cast<const uint4*>(bp)[q4];
+                const OutT* h = reinterpret_cast<const OutT*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[8 * q4 + e] += p.beta * to_f32(h[e]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) v[j] += p.beta * to_f32(brow[(col0 + j) * p.bias_sn]);
+            }
           }
           const bool vec = (p.c_sn == 1) && (col0 + 32 <= p.N) && ((reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0);
           if (vec) {

@@ -55,7 +55,10 @@ class LoRAInt8Linear(nn.Module):
 
     def forward(self, x):
         y = self.base(x)
-        return y + F.linear(F.linear(x, self.lora_down), self.lora_up) * self.scale
+        h = F.linear(x, self.lora_down)
+        # the up-projection accumulates onto the base output in one GEMM: y + (h B^T) * alpha / r
+        out = torch.addmm(y.reshape(-1, y.shape[-1]), h.reshape(-1, h.shape[-1]), self.lora_up.t(), alpha=self.scale)
+        return out.view(y.shape)
 
 
 class DiTBlock(nn.Module):
@@ -85,14 +88,17 @@ class DiTBlock(nn.Module):
         sh1, sc1, g1, sh2, sc2, g2, sh3, sc3, g3 = mod
 
         def modln(t, sh, sc):
+            if t.shape[0] == 1:  # one sample: the modulation is the LayerNorm's own affine (one kernel)
+                return F.layer_norm(t, (self.h,), weight=(1 + sc).view(self.h), bias=sh.view(self.h), eps=1e-6)
             return F.layer_norm(t, (self.h,), eps=1e-6) * (1 + sc) + sh
 
+        # residual updates x + g * branch as one addcmul kernel
         h = modln(x, sh1, sc1)
-        x = x + g1 * self._attn(h, h, h, self.q, self.k, self.v, self.o)
+        x = torch.addcmul(x, g1, self._attn(h, h, h, self.q, self.k, self.v, self.o))
         h = modln(x, sh2, sc2)
-        x = x + g2 * self._attn(h, text, text, self.cq, self.ck, self.cv, self.co)
+        x = torch.addcmul(x, g2, self._attn(h, text, text, self.cq, self.ck, self.cv, self.co))
         h = modln(x, sh3, sc3)
-        x = x + g3 * self.fc2(F.gelu(self.fc1(h), approximate="tanh"))
+        x = torch.addcmul(x, g3, self.fc2(F.gelu(self.fc1(h), approximate="tanh")))
         return x
 
 
