@@ -166,3 +166,31 @@ class LoRATrainer:
         self.opt.step()
         self.reducer.zero_grad()
         return loss.detach()
+
+    def graphed(self, x, text, cond, target, warmup=3):
+        """Single-process step with forward + backward captured once as a CUDA graph (the inputs are the
+        graph's static buffers: copy new data into them before each call) and the optimizer launched
+        after each replay. Returns a callable performing one step and returning the loss tensor."""
+        if self.reducer.world > 1:
+            raise RuntimeError("graphed(): single process only (the all-reduce hooks run on the host)")
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(x, text, cond, target)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for flat in self.reducer.flats:  # gradients accumulate into the bucket buffers
+                flat.zero_()
+            loss = F.mse_loss(self.model(x, text, cond).float(), target.float())
+            loss.backward()
+        self._graph = graph  # kept alive with its memory pool
+
+        def run():
+            graph.replay()
+            self.opt.step()
+            return loss.detach()
+
+        return run
