@@ -354,6 +354,9 @@ __global__ void __launch_bounds__(320, 1)
     }
   }
 
+  // Warps 0 and 1 reach here diverged (lane 0 ran the producer / MMA role): reconverge each warp
+  // before the CTA barrier, which is an aligned barrier and must be executed by whole warps.
+  __syncwarp();
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -768,6 +771,9 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     }
   }
 
+  // Warps 0 and 1 reach here diverged (lane 0 ran the producer / MMA role): reconverge each warp
+  // before the CTA barrier, which is an aligned barrier and must be executed by whole warps.
+  __syncwarp();
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -20,6 +20,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -92,6 +93,9 @@ struct TcParams {
   // gemm_splitk_reduce forms C. ksplit == 1: the epilogue writes C directly.
   int ksplit, kps;
   float* partial;
+  // c_tma: C is written through the tensor map tmC (32-column x 32-row boxes, 64 B swizzle) from a
+  // per-warp shared-memory staging tile; c3d: that map has a batch dimension
+  int c_tma, c3d;
 };
 
 template <int BN, int DEQ, int MSUB>
@@ -100,21 +104,28 @@ struct Cfg {
   static constexpr int A_BYTES = BMT * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int R_BYTES = DEQ ? BN * BK : 0;  // raw int8 tile
-  // bf16: a TMA stage holds A and B. int8: a TMA stage holds A and the raw int8 tile; the dequantised
-  // bf16 B tiles live in their own NB-deep ring, so the TMA ring (which must cover the load latency)
-  // is not sized by the dequant buffers.
-  static constexpr int STAGE = A_BYTES + (DEQ ? R_BYTES : B_BYTES);
-  static constexpr int NB = DEQ ? 2 : 0;
-  static constexpr int BUDGET = 224 * 1024 - NB * B_BYTES;
+  // bf16: a TMA stage holds A and B. int8: three rings. A stages (released by the MMAs), raw int8
+  // tiles (released by the dequant warps as soon as they have converted one, so those loads run
+  // ahead of the MMAs) and NB dequantised bf16 B tiles (released by the MMAs).
+  static constexpr int STAGE = A_BYTES + (DEQ ? 0 : B_BYTES);
+  static constexpr int NB = DEQ;  // int8: depth of the dequantised B ring (DEQ = 0: the bf16 path)
+  static constexpr int NR = DEQ ? (R_BYTES >= 11264 ? 3 : 4) : 0;  // int8: depth of the raw ring
+  // epilogue: per warp one staging buffer (32 rows x 32 16-bit columns) and the tile's bias row
+  static constexpr int EPI_BYTES = 4 * 2048 + 4 * 512;
+  static constexpr int BUDGET = 224 * 1024 - NB * B_BYTES - NR * R_BYTES - EPI_BYTES;
   static constexpr int STAGES = BUDGET / STAGE > 8 ? 8 : BUDGET / STAGE;
-  static constexpr int OFF_B = STAGES * STAGE;  // int8: the B ring
+  static constexpr int OFF_R = STAGES * STAGE;       // int8: the raw ring
+  static constexpr int OFF_B = OFF_R + NR * R_BYTES;  // int8: the B ring
   // int8 dequant warps run pure ALU work; they take warp ids 6-8, 10-12, 14-15 so that none shares
   // a scheduler (warp id % 4) with the MMA-issuing warp 1, whose issue slots they would otherwise
   // take (warps 9 and 13 idle).
   static constexpr int DEQ_WARPS = DEQ ? 8 : 0;
   static constexpr int THREADS = DEQ ? 16 * 32 : 6 * 32;
-  static constexpr int SMEM = OFF_B + NB * B_BYTES + 1024 + 256;
+  static constexpr int R_WARP = 13;  // int8: lane 0 of this otherwise idle warp loads the raw ring
+  static constexpr int OFF_EPI = OFF_B + NB * B_BYTES;
+  static constexpr int SMEM = OFF_EPI + EPI_BYTES + 1024 + 512;
   static_assert(SMEM <= 232448, "GEMM stages exceed the 227 KB shared-memory limit");
+  static_assert(STAGES >= 2, "GEMM needs at least two TMA stages");
   static constexpr uint32_t SUB_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per M sub-tile
   static constexpr uint32_t ACC_COLS = MSUB * SUB_COLS;  // one accumulator (all M sub-tiles)
   static constexpr int NACC = 2 * ACC_COLS <= 512 ? 2 : 1;  // double-buffered when it fits
@@ -132,34 +143,33 @@ __device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// 4 int8 (one 32-bit word) -> 4 exact fp32: bias to unsigned, splice the byte under the exponent of
-// 2^23 with a byte permute, subtract 2^23 + 128 (exact).
-__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* f) {
-  w ^= 0x80808080u;
-  f[0] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540)) - 8388736.f;
-  f[1] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541)) - 8388736.f;
-  f[2] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542)) - 8388736.f;
-  f[3] = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543)) - 8388736.f;
-}
-
 // 16 int8 * scale -> 8 words of packed bf16 (one fp32 multiply and one round-to-nearest-even each,
-// the same bits as b2_dequant_int8 for every finite product).
+// the same bits as b2_dequant_int8 for every finite product). The exact int8 -> fp32 step and the
+// scale multiply run as packed two-lane fp32 operations (each lane rounds exactly as the scalar op).
 __device__ __forceinline__ void dequant16(const int4& raw, float s, uint32_t* w) {
   const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
+  const float2 ss = make_float2(s, s);
+  const float2 bias = make_float2(-8388736.f, -8388736.f);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float f[4];
-    i8x4_to_f32(r[i], f);
-    __nv_bfloat162 lo = __floats2bfloat162_rn(f[0] * s, f[1] * s);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(f[2] * s, f[3] * s);
-    w[2 * i] = *reinterpret_cast<uint32_t*>(&lo);
-    w[2 * i + 1] = *reinterpret_cast<uint32_t*>(&hi);
+    const uint32_t u = r[i] ^ 0x80808080u;
+    float2 lo = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)));
+    float2 hi = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)));
+    lo = __fmul2_rn(__fadd2_rn(lo, bias), ss);
+    hi = __fmul2_rn(__fadd2_rn(hi, bias), ss);
+    __nv_bfloat162 blo = __floats2bfloat162_rn(lo.x, lo.y);
+    __nv_bfloat162 bhi = __floats2bfloat162_rn(hi.x, hi.y);
+    w[2 * i] = *reinterpret_cast<uint32_t*>(&blo);
+    w[2 * i + 1] = *reinterpret_cast<uint32_t*>(&bhi);
   }
 }
 
 template <int BN, bool BF16, int DEQ, int MSUB>
 __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, TcParams p) {
   using C = Cfg<BN, DEQ, MSUB>;
   constexpr int S = C::STAGES;
   constexpr int NDQ = C::DEQ_WARPS * 32;
@@ -167,14 +177,17 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int NB = C::NB > 0 ? C::NB : 1;
   constexpr int NACC = C::NACC;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_B + C::NB * C::B_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_EPI + C::EPI_BYTES);
   uint64_t* full = bars;                // [S]  TMA landed
   uint64_t* empty = bars + S;           // [S]  MMA done reading the stage
   uint64_t* tfull = bars + 2 * S;       // [2]  accumulator ready
   uint64_t* tempty = bars + 2 * S + 2;  // [2]  accumulator drained
   uint64_t* bready = bars + 2 * S + 4;       // [NB] (int8) B buffer dequantised
   uint64_t* bfree = bars + 2 * S + 4 + NB;   // [NB] (int8) MMAs reading the B buffer done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4 + 2 * NB);
+  constexpr int NR = C::NR > 0 ? C::NR : 1;
+  uint64_t* rfull = bars + 2 * S + 4 + 2 * NB;        // [NR] (int8) raw tile landed
+  uint64_t* rempty = bars + 2 * S + 4 + 2 * NB + NR;  // [NR] (int8) raw tile converted
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4 + 2 * NB + 2 * NR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -187,8 +200,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       tc::mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < NB; ++i) {
-      tc::mbar_init(&bready[i], NDQ > 0 ? NDQ : 1);
+      tc::mbar_init(&bready[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS : 1);  // one arrival per dequant warp
       tc::mbar_init(&bfree[i], 1);
+    }
+    for (int i = 0; i < NR; ++i) {
+      tc::mbar_init(&rfull[i], 1);
+      tc::mbar_init(&rempty[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS : 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&tfull[i], 1);
@@ -225,6 +242,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     if (lane == 0) {
       tc::tma_prefetch_desc(&tmA);
       tc::tma_prefetch_desc(&tmB);
+      if (p.c_tma) tc::tma_prefetch_desc(&tmC);
       int stage = 0;
       uint32_t phase = 0;
       int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -241,7 +259,6 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
           uint8_t* sa = smem + stage * C::STAGE;
           uint8_t* sb = sa + C::A_BYTES;
-          uint8_t* sr = sa + C::A_BYTES;  // int8: the raw tile follows A
           const uint32_t bytes = C::STAGE;
           tc::mbar_arrive_expect_tx(&full[stage], bytes);
           const int k0 = kb * BK;
@@ -256,9 +273,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
             }
           }
           if (DEQ) {
-            // raw int8 W tile: forward box {64 (k), BN (n)}; transposed box {BN (k_feat), 64 (n_feat)}
-            if (!p.b_mn) tc::tma_load_2d(sr, &tmB, &full[stage], k0, n0);
-            else tc::tma_load_2d(sr, &tmB, &full[stage], n0, k0);
+            // the raw int8 W tiles have their own ring and producer
           } else if (!p.b_mn) {
             if (p.b3d) tc::tma_load_3d(sb, &tmB, &full[stage], k0, n0, b);
             else tc::tma_load_2d(sb, &tmB, &full[stage], k0, n0);
@@ -344,52 +359,141 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
   } else if (warp < 6) {
     // ------------------------------- epilogue -----------------------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* stg = smem + C::OFF_EPI + (warp - 2) * 2048;  // this warp's staging buffer
     int it = 0;
     using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    // a bias that is one row broadcast over M (addmm's usual form) is copied to shared memory per
+    // tile before the accumulator is ready, so that its load latency overlaps the mainloop
+    OutT* bsm = reinterpret_cast<OutT*>(smem + C::OFF_EPI + 4 * 2048 + (warp - 2) * 512);
+    const bool bias_row = p.has_bias && p.bias_sm == 0 && (p.batch == 1 || p.bias_sb == 0) && p.bias_sn == 1 &&
+                          (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
     for (int t = blockIdx.x; t < total_work; t += gridDim.x, ++it) {
       const int acc = it % NACC;
+      int m0, n0, b;
+      tile_coords(t, m0, n0, b);
+      if (bias_row) {
+        const OutT* bsrc = (const OutT*)p.bias + n0;
+        for (int c = lane; c < BN / 8; c += 32) {
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (n0 + c * 8 + 8 <= p.N) {
+            v = *reinterpret_cast<const uint4*>(bsrc + c * 8);
+          } else {
+            OutT* h = reinterpret_cast<OutT*>(&v);
+            for (int e = 0; e < 8; ++e)
+              if (n0 + c * 8 + e < p.N) h[e] = bsrc[c * 8 + e];
+          }
+          *reinterpret_cast<uint4*>(bsm + c * 8) = v;
+        }
+        __syncwarp();
+      }
       if (!tc::mbar_wait(&tfull[acc], (it / NACC) & 1, p.err) || *abort_flag) {
         *abort_flag = 1;
         break;
       }
       tc::tc_fence_after();
-      int m0, n0, b;
-      tile_coords(t, m0, n0, b);
 #pragma unroll 1
       for (int ms = 0; ms < MSUB; ++ms) {
         const int64_t row = m0 + ms * BM + q * 32 + lane;
         const bool row_ok = row < p.M;
         OutT* crow = (OutT*)p.c + b * p.c_sb + row * p.c_sm;
         const OutT* brow = (const OutT*)p.bias + b * p.bias_sb + row * p.bias_sm;
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
-          uint32_t r[32];
+        // one chunk of W (32 or 16) accumulator columns: TMEM -> registers -> C (or the split-K partial)
+        auto chunk = [&](auto wc, int cc) {
+          constexpr int W = decltype(wc)::value;
+          uint32_t r[W];
           __syncwarp();
-          tc::tmem_ld32(tbase + (uint32_t)(acc * C::ACC_COLS + ms * C::SUB_COLS + ch * 32) + ((uint32_t)(q * 32) << 16), r);
+          const uint32_t taddr = tbase + (uint32_t)(acc * C::ACC_COLS + ms * C::SUB_COLS + cc) + ((uint32_t)(q * 32) << 16);
+          if constexpr (W == 32) tc::tmem_ld32(taddr, r);
+          else tc::tmem_ld16(taddr, r);
           tc::tmem_wait_ld();
-          const int64_t col0 = n0 + ch * 32;
-          if (!row_ok || col0 >= p.N) continue;
+          const int64_t col0 = n0 + cc;
+          if (col0 >= p.N) return;  // warp-uniform
+          if constexpr (W == 32) {
+            if (p.c_tma && !p.partial) {
+              // bias / alpha in registers, bf16 row into the swizzled staging tile, one TMA store
+              // of the warp's 32 x 32 box (rows past M and columns past N are clipped by the store)
+              // in place: r[j] holds the fp32 bits of alpha * acc + beta * bias
+#pragma unroll
+              for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(p.alpha * __uint_as_float(r[j]));
+              if (bias_row) {
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                  const uint4 raw = reinterpret_cast<const uint4*>(bsm + cc)[q4];
+                  const OutT* h = reinterpret_cast<const OutT*>(&raw);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e)
+                    r[8 * q4 + e] = __float_as_uint(__uint_as_float(r[8 * q4 + e]) + p.beta * to_f32(h[e]));
+                }
+              } else if (p.has_bias && row_ok) {
+                const OutT* bp = brow + col0 * p.bias_sn;
+                if (p.bias_sn == 1 && col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {
+#pragma unroll
+                  for (int q4 = 0; q4 < 4; ++q4) {
+                    const uint4 raw = reinterpret_cast<const uint4*>(bp)[q4];
+                    const OutT* h = reinterpret_cast<const OutT*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                      r[8 * q4 + e] = __float_as_uint(__uint_as_float(r[8 * q4 + e]) + p.beta * to_f32(h[e]));
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (col0 + j < p.N)
+                      r[j] = __float_as_uint(__uint_as_float(r[j]) + p.beta * to_f32(brow[(col0 + j) * p.bias_sn]));
+                }
+              }
+              uint8_t* buf = stg;
+              if (lane == 0) tc::bulk_wait_read0();  // the previous chunk's store has read the buffer
+              __syncwarp();
+              uint8_t* rowp = buf + lane * 64;
+#pragma unroll
+              for (int j = 0; j < 4; ++j)  // 64 B swizzle: 16 B chunk j of row r at (j ^ ((r >> 1) & 3))
+                *reinterpret_cast<uint4*>(rowp + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                    make_uint4(pack_out(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1]), BF16),
+                               pack_out(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]), BF16),
+                               pack_out(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]), BF16),
+                               pack_out(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]), BF16));
+              tc::fence_async_shared();
+              __syncwarp();
+              if (lane == 0) {
+                const int32_t r0 = (int32_t)(m0 + ms * BM + q * 32);
+                if (p.c3d) tc::tma_store_3d(&tmC, buf, (int32_t)col0, r0, b);
+                else tc::tma_store_2d(&tmC, buf, (int32_t)col0, r0);
+                tc::bulk_commit();
+              }
+              return;
+            }
+          }
+          if (!row_ok) return;
           if (p.partial) {  // split-K partial tile, fp32 [split][M][N]
             float* prow = p.partial + ((int64_t)(t / total_tiles) * p.M + row) * p.N + col0;
-            if (col0 + 32 <= p.N && (p.N & 3) == 0) {
+            if (col0 + W <= p.N && (p.N & 3) == 0) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
+              for (int j = 0; j < W / 4; ++j)
                 reinterpret_cast<float4*>(prow)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                                                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
             } else {
-              for (int j = 0; j < 32 && col0 + j < p.N; ++j) prow[j] = __uint_as_float(r[j]);
+              for (int j = 0; j < W && col0 + j < p.N; ++j) prow[j] = __uint_as_float(r[j]);
             }
-            continue;
+            return;
           }
-          float v[32];
+          float v[W];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
-          if (p.has_bias) {
+          for (int j = 0; j < W; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+          if (bias_row) {
+#pragma unroll
+            for (int q4 = 0; q4 < W / 8; ++q4) {
+              const uint4 raw = reinterpret_cast<const uint4*>(bsm + cc)[q4];
+              const OutT* h = reinterpret_cast<const OutT*>(&raw);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[8 * q4 + e] += p.beta * to_f32(h[e]);
+            }
+          } else if (p.has_bias) {
             const OutT* bp = brow + col0 * p.bias_sn;
-            if (p.bias_sn == 1 && col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {
-              // a contiguous bias row segment (addmm with a full-matrix or broadcast-row bias): 4 x 16 B
+            if (p.bias_sn == 1 && col0 + W <= p.N && (reinterpret_cast<uintptr_t>(bp) & 15) == 0) {
+              // a contiguous bias row segment (addmm with a full-matrix or broadcast-row bias): 16 B loads
 #pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
+              for (int q4 = 0; q4 < W / 8; ++q4) {
                 const uint4 raw = reinterpret_cast<const uint4*>(bp)[q4];
                 const OutT* h = reinterpret_cast<const OutT*>(&raw);
 #pragma unroll
@@ -397,33 +501,68 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
               }
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
+              for (int j = 0; j < W; ++j)
                 if (col0 + j < p.N) v[j] += p.beta * to_f32(brow[(col0 + j) * p.bias_sn]);
             }
           }
-          const bool vec = (p.c_sn == 1) && (col0 + 32 <= p.N) && ((reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0);
+          const bool vec = (p.c_sn == 1) && (col0 + W <= p.N) && ((reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0);
           if (vec) {
             uint4* dst = reinterpret_cast<uint4*>(crow + col0);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < W / 8; ++j)
               dst[j] = make_uint4(pack_out(v[8 * j], v[8 * j + 1], BF16), pack_out(v[8 * j + 2], v[8 * j + 3], BF16),
                                   pack_out(v[8 * j + 4], v[8 * j + 5], BF16), pack_out(v[8 * j + 6], v[8 * j + 7], BF16));
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < W; ++j)
               if (col0 + j < p.N) crow[(col0 + j) * p.c_sn] = from_f32<OutT>(v[j]);
           }
-        }
+        };
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) chunk(std::integral_constant<int, 32>{}, ch * 32);
+        if constexpr (BN % 32 != 0) chunk(std::integral_constant<int, 16>{}, (BN / 32) * 32);
       }
       tc::tc_fence_before();
       tc::mbar_arrive(&tempty[acc]);
+    }
+    if (lane == 0) tc::bulk_wait0();  // every C store of this warp complete before the CTA exits
+  } else if (DEQ && warp == C::R_WARP) {
+    // ------------------------------- int8 raw-tile producer ----------------------------------
+    if (lane == 0) {
+      int rs = 0;
+      uint32_t rph = 0;
+      int issued[4] = {0, 0, 0, 0};
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x) {
+        int m0, n0, b, kb0, kb1;
+        tile_coords(t, m0, n0, b);
+        k_range(t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!tc::mbar_wait(&rempty[rs], rph ^ 1, p.err) || *abort_flag) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* sr = smem + C::OFF_R + rs * C::R_BYTES;
+          tc::mbar_arrive_expect_tx(&rfull[rs], (uint32_t)C::R_BYTES);
+          // raw int8 W tile: forward box {64 (k), BN (n)}; transposed box {BN (k_feat), 64 (n_feat)}
+          if (!p.b_mn) tc::tma_load_2d(sr, &tmB, &rfull[rs], kb * BK, n0);
+          else tc::tma_load_2d(sr, &tmB, &rfull[rs], n0, kb * BK);
+          issued[rs] += 1;
+          if (++rs == NR) {
+            rs = 0;
+            rph ^= 1;
+          }
+        }
+      }
+      if (!ok)
+        for (int r = 0; r < NR; ++r)
+          if (issued[r] > 0) tc::mbar_wait(&rfull[r], (uint32_t)((issued[r] - 1) & 1), nullptr);
     }
   } else if (DEQ && (warp & 3) != 1) {
     // ------------------------------- int8 dequant -------------------------------------------
     const int dw = warp - 6 - (warp > 9 ? 1 : 0) - (warp > 13 ? 1 : 0);  // 0 .. 7
     const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
-    int stage = 0;
-    uint32_t phase = 0;
     int gk = 0;  // K blocks dequantised so far (B ring position)
     constexpr int FIPT = (BN * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
     float fsc[FIPT];
@@ -433,7 +572,22 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       k_range(t, kb0, kb1);
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!tc::mbar_wait(&full[stage], phase, p.err) || *abort_flag) {
+        // forward scales, loaded before the waits so that their latency overlaps them: block-64
+        // scales change with the K block, per-row scales are loaded once per tile
+        if (!p.b_mn && (p.scale_layout == 0 || kb == kb0)) {
+#pragma unroll
+          for (int u = 0; u < FIPT; ++u) {  // every scale load in flight before the first is used
+            const int i = dt + u * NDQ;
+            const int64_t gn = (int64_t)n0 + (i >> 2);
+            fsc[u] = 0.f;
+            if (i < BN * 4 && gn < p.deq_rows)
+              fsc[u] = p.scale_layout == 0
+                           ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
+                           : reinterpret_cast<const float*>(p.scale)[gn];
+          }
+        }
+        const int rs = gk % NR;
+        if (!tc::mbar_wait(&rfull[rs], (uint32_t)((gk / NR) & 1), p.err) || *abort_flag) {
           ok = false;
           break;
         }
@@ -443,23 +597,10 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           break;
         }
         uint8_t* sb = smem + C::OFF_B + bb * C::B_BYTES;
-        const uint8_t* sr = smem + stage * C::STAGE + C::A_BYTES;
+        const uint8_t* sr = smem + C::OFF_R + rs * C::R_BYTES;
         if (!p.b_mn) {
           // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
-          // block-64 scales change with the K block; per-row scales were loaded once for the tile
-          if (p.scale_layout == 0 || kb == kb0) {
-#pragma unroll
-            for (int u = 0; u < FIPT; ++u) {  // every scale load in flight before the first is used
-              const int i = dt + u * NDQ;
-              const int64_t gn = (int64_t)n0 + (i >> 2);
-              fsc[u] = 0.f;
-              if (i < BN * 4 && gn < p.deq_rows)
-                fsc[u] = p.scale_layout == 0
-                             ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
-                             : reinterpret_cast<const float*>(p.scale)[gn];
-            }
-          }
 #pragma unroll
           for (int u = 0; u < FIPT; ++u) {
             const int i = dt + u * NDQ;
@@ -506,18 +647,23 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
             *reinterpret_cast<uint4*>(rowp + (((g0 + 1) ^ (i & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
           }
         }
+        // every thread's B stores visible to the tensor core's (async proxy) reads; the raw tile and
+        // the B buffer are signalled once per warp
         tc::fence_async_shared();
-        tc::mbar_arrive(&bready[bb]);
-        ++gk;
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1;
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&rempty[rs]);
+          tc::mbar_arrive(&bready[bb]);
         }
+        ++gk;
       }
       if (!ok) break;
     }
   }
 
+  // Warps 0 and 1 reach here diverged (lane 0 ran the producer / MMA role): reconverge each warp
+  // before the CTA barrier, which is an aligned barrier and must be executed by whole warps.
+  __syncwarp();
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -532,7 +678,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
 bool tma_ok_stride(int64_t s_elems, int esz) { return ((s_elems * esz) % 16) == 0; }
 
 template <int BN, bool BF16, int DEQ, int MSUB>
-int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t st, const char* name) {
+int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc_, const TcParams& p, cudaStream_t st,
+                  const char* name) {
   using C = Cfg<BN, DEQ, MSUB>;
   static bool attr_set = false;  // set once per process (single device per process)
   if (!attr_set) {
@@ -545,7 +692,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& 
   int tiles = p.m_tiles * p.n_tiles * (int)p.batch * p.ksplit;
   int grid = std::min(tiles, device_info().sm_count);
   LaunchScope ls(name, st);
-  gemm_tc_kernel<BN, BF16, DEQ, MSUB><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
+  gemm_tc_kernel<BN, BF16, DEQ, MSUB><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, tc_, p);
   return after_launch(name);
 }
 
@@ -607,6 +754,23 @@ TileChoice pick_tile(int64_t M, int64_t N, int64_t batch) {
   return best;
 }
 
+// Tensor map for the output C (16-bit, unit column stride): boxes of 32 columns x 32 rows with the
+// 64 B swizzle the epilogue's staging tiles use. Sets p.c_tma / p.c3d; leaves them 0 (direct
+// stores) when C's layout cannot be described (strided columns, unaligned rows) or the GEMM writes
+// split-K partials.
+void setup_cmap(CUtensorMap* tm, CUtensorMapDataType dt, TcParams& p) {
+  p.c_tma = 0, p.c3d = 0;
+  if (p.ksplit > 1 || p.c_sn != 1 || ((uintptr_t)p.c & 15)) return;
+  if (p.M > 1 && (p.c_sm * 2) % 16) return;
+  const bool b3 = p.batch > 1;
+  if (b3 && (p.c_sb == 0 || (p.c_sb * 2) % 16)) return;
+  uint64_t dims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batch};
+  uint64_t strides[2] = {(uint64_t)(p.M > 1 ? p.c_sm : ((p.N + 7) / 8) * 8) * 2, (uint64_t)p.c_sb * 2};
+  uint32_t box[3] = {32, 32, 1};
+  if (!make_tmap(tm, dt, b3 ? 3 : 2, p.c, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) return;
+  p.c_tma = 1, p.c3d = b3 ? 1 : 0;
+}
+
 }  // namespace
 
 bool gemm_tc_eligible(const b2_gemm_args* a) {
@@ -658,6 +822,9 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
         ((uintptr_t)a->workspace & 15) == 0)
       p.ksplit = ks, p.kps = kps, p.partial = (float*)a->workspace;
   }
+  CUtensorMap tcm;
+  memset(&tcm, 0, sizeof(tcm));
+  setup_cmap(&tcm, dt, p);
 
   CUtensorMap ta, tb;
   {
@@ -694,14 +861,14 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
   }
   int rc;
   if (BN == 256 && tc_.msub == 2)
-    rc = bf16 ? launch_kernel<256, true, 0, 2>(ta, tb, p, st, "gemm_tc_256x256")
-              : launch_kernel<256, false, 0, 2>(ta, tb, p, st, "gemm_tc_256x256");
+    rc = bf16 ? launch_kernel<256, true, 0, 2>(ta, tb, tcm, p, st, "gemm_tc_256x256")
+              : launch_kernel<256, false, 0, 2>(ta, tb, tcm, p, st, "gemm_tc_256x256");
   else if (BN == 256)
-    rc = bf16 ? launch_kernel<256, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn256")
-              : launch_kernel<256, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn256");
+    rc = bf16 ? launch_kernel<256, true, 0, 1>(ta, tb, tcm, p, st, "gemm_tc_bn256")
+              : launch_kernel<256, false, 0, 1>(ta, tb, tcm, p, st, "gemm_tc_bn256");
   else
-    rc = bf16 ? launch_kernel<128, true, 0, 1>(ta, tb, p, st, "gemm_tc_bn128")
-              : launch_kernel<128, false, 0, 1>(ta, tb, p, st, "gemm_tc_bn128");
+    rc = bf16 ? launch_kernel<128, true, 0, 1>(ta, tb, tcm, p, st, "gemm_tc_bn128")
+              : launch_kernel<128, false, 0, 1>(ta, tb, tcm, p, st, "gemm_tc_bn128");
   if (rc || p.ksplit == 1) return rc;
   const int64_t total = a->M * a->N;
   const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)device_info().sm_count * 8);
@@ -748,14 +915,16 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   cudaStream_t st = (cudaStream_t)stream;
   // Tile choice. The dequant work per FLOP is 1/(2*rows of the CTA tile), so two stacked M=128 UMMA
   // tiles (256 rows) halve it; among the shapes the kernel supports, take the one with the best
-  // wave-quantised SM utilisation, weighted by how well the dequant warps keep up.
+  // wave-quantised SM utilisation, weighted by how well the dequant warps keep up. The 176-wide tile
+  // (forward only: the transposed form dequantises 64-column chunks) puts M = 1024, N = 6144 on
+  // 140 CTAs, one wave.
   struct Choice { int bn, msub; double eff; };
-  const Choice fwd_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const Choice fwd_opts[] = {{256, 2, 1.15}, {176, 2, 1.08}, {128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
   const Choice dx_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
   const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
   Choice best{0, 0, -1.0};
   double best_score = -1.0;
-  const int nopts = a->transpose_w ? 4 : 5;
+  const int nopts = a->transpose_w ? 4 : 6;
   static const int forced = [] {  // B2_INT8_TILE=<bn>x<msub> pins the tile (measurement sweeps)
     const char* e = getenv("B2_INT8_TILE");
     int bn = 0, ms = 0;
@@ -784,6 +953,9 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   p.err = device_error_ptr();
   p.scale = a->scale, p.scale_layout = a->scale_layout, p.scale_nb = (a->K + 63) / 64, p.deq_rows = a->N;
   p.ksplit = 1, p.kps = p.k_blocks;
+  CUtensorMap tcm;
+  memset(&tcm, 0, sizeof(tcm));
+  setup_cmap(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p);
   CUtensorMap ta, tb;
   {
     uint64_t dims[2] = {(uint64_t)red, (uint64_t)a->M}, strides[1] = {(uint64_t)a->x_ld * 2};
@@ -800,9 +972,10 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
       return fail(B2_ERR_ARG, "int8_gemm: tensor map for q rejected");
   }
   const char* name = a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd";
-  if (best.msub == 2 && BN == 256) return launch_kernel<256, true, 1, 2>(ta, tb, p, st, name);
-  if (best.msub == 2 && BN == 128) return launch_kernel<128, true, 1, 2>(ta, tb, p, st, name);
-  if (best.msub == 2 && BN == 96) return launch_kernel<96, true, 1, 2>(ta, tb, p, st, name);
-  if (BN == 256) return launch_kernel<256, true, 1, 1>(ta, tb, p, st, name);
-  return launch_kernel<128, true, 1, 1>(ta, tb, p, st, name);
+  if (best.msub == 2 && BN == 256) return launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name);
+  if (best.msub == 2 && BN == 176) return launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name);
+  if (best.msub == 2 && BN == 128) return launch_kernel<128, true, 2, 2>(ta, tb, tcm, p, st, name);
+  if (best.msub == 2 && BN == 96) return launch_kernel<96, true, 2, 2>(ta, tb, tcm, p, st, name);
+  if (BN == 256) return launch_kernel<256, true, 2, 1>(ta, tb, tcm, p, st, name);
+  return launch_kernel<128, true, 2, 1>(ta, tb, tcm, p, st, name);
 }

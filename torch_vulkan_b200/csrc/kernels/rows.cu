@@ -378,6 +378,24 @@ int softmax_entry(const b2_softmax_args* a, b2_stream_t stream, bool fwd) {
 
 // ================================== layer norm ===================================================
 
+// Two sums in one pass of the group reduction (`red` holds >= 64 floats).
+template <int GROUP>
+__device__ __forceinline__ void group_sum2(float& a, float& b, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if (GROUP == 32) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, g0 = (threadIdx.x / GROUP) * (GROUP / 32);
+  __syncthreads();
+  if (lane == 0) red[w] = a, red[32 + w] = b;
+  __syncthreads();
+  a = red[g0], b = red[32 + g0];
+#pragma unroll
+  for (int i = 1; i < GROUP / 32; ++i) a += red[g0 + i], b += red[32 + g0 + i];
+}
+
 template <typename T, int GROUP, int V, int NCH>
 __global__ void __launch_bounds__(256) ln_fwd_reg(const T* __restrict__ x, const T* __restrict__ w,
                                                   const T* __restrict__ b, T* __restrict__ y, float* __restrict__ mean,
@@ -446,7 +464,7 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
                                                   const T* __restrict__ g, const float* __restrict__ mean,
                                                   const float* __restrict__ rstd, T* __restrict__ dx,
                                                   float* __restrict__ part, int64_t rows, int64_t D) {
-  __shared__ float red[32];
+  __shared__ float red[64];
   const int rpb = blockDim.x / GROUP;
   const int t = threadIdx.x % GROUP;
   const float invD = 1.f / (float)D;
@@ -499,8 +517,8 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
       }
     }
     fetch(row + stride);
-    s1 = group_sum<GROUP>(s1, red) * invD;
-    s2 = group_sum<GROUP>(s2, red) * invD;
+    group_sum2<GROUP>(s1, s2, red);
+    s1 *= invD, s2 *= invD;
     if (!active || !dx) continue;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
@@ -513,6 +531,9 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
       }
     }
   }
+  // the weight-gradient reduction (launched as a programmatic dependent) may start its prologue; its
+  // griddepcontrol.wait still sees every partial written below
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (part) {
     int64_t slot = (int64_t)blockIdx.x * rpb + threadIdx.x / GROUP;
     float* pw = part + slot * 2 * D;
@@ -537,18 +558,28 @@ __global__ void __launch_bounds__(1024) ln_wgrad_reduce(const float* __restrict_
                                                         T* __restrict__ dw, T* __restrict__ db) {
   __shared__ float sw[32][33], sb[32][33];
   const int64_t col = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the partials of the preceding backward kernel
   float aw0 = 0.f, ab0 = 0.f, aw1 = 0.f, ab1 = 0.f;
   if (col < D) {
+    const float* pc = part + col;
     int64_t s = threadIdx.y;
-    for (; s + 32 < nslots; s += 64) {
-      aw0 += part[s * 2 * D + col];
-      ab0 += part[s * 2 * D + D + col];
-      aw1 += part[(s + 32) * 2 * D + col];
-      ab1 += part[(s + 32) * 2 * D + D + col];
+    // eight slots per thread per pass, all sixteen loads issued before the first add
+    for (; s + 7 * 32 < nslots; s += 8 * 32) {
+      float lw[8], lb[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        lw[u] = pc[(s + 32 * u) * 2 * D];
+        lb[u] = pc[(s + 32 * u) * 2 * D + D];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u += 2) {
+        aw0 += lw[u], ab0 += lb[u];
+        aw1 += lw[u + 1], ab1 += lb[u + 1];
+      }
     }
-    if (s < nslots) {
-      aw0 += part[s * 2 * D + col];
-      ab0 += part[s * 2 * D + D + col];
+    for (; s < nslots; s += 32) {
+      aw0 += pc[s * 2 * D];
+      ab0 += pc[s * 2 * D + D];
     }
   }
   sw[threadIdx.y][threadIdx.x] = aw0 + aw1;
@@ -749,9 +780,9 @@ int ln_run(const b2_layernorm_args* a, cudaStream_t st, bool fwd) {
     }
   }
   if (want_w) {
-    LaunchScope ls("layernorm_wgrad_reduce", st);
-    dim3 block(32, 32);
-    ln_wgrad_reduce<T><<<(unsigned)((a->D + 31) / 32), block, 0, st>>>(part, p.nslots, a->D, (T*)a->dw, (T*)a->db);
+    if (int rc = launch_pdl("layernorm_wgrad_reduce", ln_wgrad_reduce<T>, dim3((unsigned)((a->D + 31) / 32)), dim3(32, 32),
+                            0, st, (const float*)part, p.nslots, a->D, (T*)a->dw, (T*)a->db))
+      return rc;
   }
   return after_launch(fwd ? "b2_layernorm_fwd" : "b2_layernorm_bwd");
 }
