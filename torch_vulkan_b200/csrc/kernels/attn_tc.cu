@@ -18,6 +18,7 @@
 //           converted at the end.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code and unwinds.
 #include <cuda.h>
+#include <cstring>
 
 #include <type_traits>
 
@@ -90,7 +91,7 @@ struct FwdCfg {
 template <int D, bool BF16>
 __global__ void __launch_bounds__(320, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
+                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, AttnTcParams p) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -320,8 +321,9 @@ __global__ void __launch_bounds__(320, 1)
       const float L = x0.y * a0 + x1.y * a1;
       const float s0 = a0 / L, s1 = a1 / L;
       const int64_t qrow = q0 + r;
-      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      T* orow = (T*)p.o + (int64_t)b * p.o_s[0] + (int64_t)h * p.o_s[1] + qrow * p.o_s[2];
+      // O rows go through a per-warp staging tile in the (now idle) K ring: 32 rows x 32 columns per
+      // box, 64-byte swizzle, one TMA store each (rows past Sq are clipped by the store)
+      uint8_t* stg = smem + C::OFF_K + (warp - 2) * (D / 64) * 2048;
 #pragma unroll
       for (int cc = 0; cc < D / 64; ++cc) {
         const int c = g * (D / 64) + cc;  // this group's 32-column chunks
@@ -332,22 +334,29 @@ __global__ void __launch_bounds__(320, 1)
         tc::tmem_wait_ld();
         tc::reg_fence32(o0);
         if (nb1 > 0) tc::reg_fence32(o1);
-        if (qrow < p.Sq) {
-          uint32_t w[16];
+        uint32_t w[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float v0 = __uint_as_float(o0[2 * e]) * s0, v1 = __uint_as_float(o0[2 * e + 1]) * s0;
-            if (nb1 > 0) {
-              v0 += __uint_as_float(o1[2 * e]) * s1;
-              v1 += __uint_as_float(o1[2 * e + 1]) * s1;
-            }
-            w[e] = pack2(v0, v1, BF16);
+        for (int e = 0; e < 16; ++e) {
+          float v0 = __uint_as_float(o0[2 * e]) * s0, v1 = __uint_as_float(o0[2 * e + 1]) * s0;
+          if (nb1 > 0) {
+            v0 += __uint_as_float(o1[2 * e]) * s1;
+            v1 += __uint_as_float(o1[2 * e + 1]) * s1;
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+          w[e] = pack2(v0, v1, BF16);
+        }
+        uint8_t* buf = stg + cc * 2048;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        for (int e = 0; e < 4; ++e)  // 16 B chunk e of row `lane` at (e ^ ((lane >> 1) & 3))
+          *reinterpret_cast<uint4*>(buf + lane * 64 + ((e ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        tc::fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_4d(&tmO, buf, c * 32, (int32_t)(q0 + quarter * 32), h, b);
+          tc::bulk_commit();
         }
       }
+      if (lane == 0) tc::bulk_wait0();
       if (g == 0 && qrow < p.Sq) p.lse[(int64_t)bh * p.Sq + qrow] = (M + __log2f(L)) * 0.6931471805599453f;
     } else {
       *abort_flag = 1;
@@ -368,16 +377,17 @@ __global__ void __launch_bounds__(320, 1)
 
 // ---- tensor maps over [B, H, S, D] with arbitrary (b, h, s) strides -----------------------------
 bool make_bhsd_map(CUtensorMap* m, const void* base, const int64_t* s3, int64_t B, int64_t H, int64_t S, int64_t D,
-                   bool bf16, uint32_t box_rows) {
+                   bool bf16, uint32_t box_rows, uint32_t box_inner = 64,
+                   CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
   uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
   uint64_t strides[3] = {(uint64_t)s3[2] * 2, (uint64_t)s3[1] * 2, (uint64_t)s3[0] * 2};
   // size-1 dims: any valid stride
   if (S == 1) strides[0] = (uint64_t)D * 2;
   if (H == 1) strides[1] = strides[0] * (uint64_t)S;
   if (B == 1) strides[2] = strides[1] * (uint64_t)H;
-  uint32_t box[4] = {64, box_rows, 1, 1};
+  uint32_t box[4] = {box_inner, box_rows, 1, 1};
   return make_tmap(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims,
-                   strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+                   strides, box, sw);
 }
 
 bool strides_ok(const int64_t* s3, int64_t B, int64_t H, int64_t S) {
@@ -411,10 +421,11 @@ int launch_fwd(const b2_attn_args* a, cudaStream_t st) {
       return rc;
     attr = true;
   }
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, D, BF16, 128) ||
       !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, D, BF16, 128) ||
-      !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, D, BF16, 128))
+      !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, D, BF16, 128) ||
+      !make_bhsd_map(&to, a->o, a->o_s, a->B, a->H, a->Sq, D, BF16, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(B2_ERR_ARG, "attn_tc: tensor map rejected");
   AttnTcParams p{};
   p.B = a->B, p.H = a->H, p.Sq = a->Sq, p.Sk = a->Sk;
@@ -425,7 +436,7 @@ int launch_fwd(const b2_attn_args* a, cudaStream_t st) {
   p.lse = a->lse;
   p.err = device_error_ptr();
   dim3 grid((unsigned)((a->Sq + 127) / 128), (unsigned)(a->B * a->H));
-  return launch_pdl("attn_fwd_tc", attn_fwd_tc<D, BF16>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, p);
+  return launch_pdl("attn_fwd_tc", attn_fwd_tc<D, BF16>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, to, p);
 }
 
 int attn_tc_fwd(const b2_attn_args* a, cudaStream_t st) {
@@ -474,7 +485,8 @@ struct BwdCfg {
 __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                       const __grid_constant__ CUtensorMap tmDQ, AttnTcParams p, const float2* __restrict__ lsed,
+                       const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmDK,
+                       const __grid_constant__ CUtensorMap tmDV, AttnTcParams p, const float2* __restrict__ lsed,
                        int64_t sq_pad) {
   using C = BwdCfg;
   constexpr bool BF16 = true;
@@ -744,10 +756,11 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     // ---------------- dK, dV epilogue: group g writes d columns [32g, 32g+32) ----------------
     if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
       tc::tc_fence_after();
-      const int64_t krow = k0 + r;
+      // rows go through a per-warp staging tile in the (now idle) Q / dO rings: 32 rows x 32 columns
+      // per box, 64-byte swizzle, one TMA store each (rows past Sk are clipped by the store)
+      uint8_t* estg = smem + C::OFF_Q + (warp - 2) * 4096;
       for (int which = 0; which < 2; ++which) {  // 0: dV, 1: dK (times scale)
         void* base = which ? p.dk : p.dv;
-        const int64_t* st = which ? p.dk_s : p.dv_s;
         const float mul = which ? p.scale : 1.f;
         const uint32_t tcol = which ? C::T_DK : C::T_DV;
         uint32_t v[32];
@@ -755,17 +768,25 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
         tc::tmem_ld32(tbase + tcol + g * 32 + lane_off, v);
         tc::tmem_wait_ld();
         tc::reg_fence32(v);
-        if (base && krow < p.Sk) {
+        if (base) {
           uint32_t w[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             w[e] = pack2(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul, BF16);
-          uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + (int64_t)b * st[0] +
-                                               (int64_t)h * st[1] + krow * st[2] + g * 32);
+          uint8_t* buf = estg + which * 2048;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          for (int e = 0; e < 4; ++e)  // 16 B chunk e of row `lane` at (e ^ ((lane >> 1) & 3))
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((e ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          tc::fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tc::tma_store_4d(which ? &tmDK : &tmDV, buf, g * 32, (int32_t)(k0 + quarter * 32), h, b);
+            tc::bulk_commit();
+          }
         }
       }
+      if (lane == 0) tc::bulk_wait0();
     } else {
       *abort_flag = 1;
     }
@@ -917,6 +938,13 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
       !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, 128, true, 128) ||
       !make_bhsd_map(&tdo, a->d_o, a->do_s, a->B, a->H, a->Sq, 128, true, 64))
     return fail(B2_ERR_ARG, "attn_bwd_tc: tensor map rejected");
+  // dK / dV (when requested) are written by TMA stores of 32 x 32 boxes
+  CUtensorMap tdk, tdv;
+  memset(&tdk, 0, sizeof(tdk));
+  memset(&tdv, 0, sizeof(tdv));
+  if ((a->dk && !make_bhsd_map(&tdk, a->dk, a->dk_s, a->B, a->H, a->Sk, 128, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) ||
+      (a->dv && !make_bhsd_map(&tdv, a->dv, a->dv_s, a->B, a->H, a->Sk, 128, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return fail(B2_ERR_ARG, "attn_bwd_tc: dK / dV tensor map rejected");
   AttnTcParams p{};
   p.B = a->B, p.H = a->H, p.Sq = a->Sq, p.Sk = a->Sk;
   p.scale = a->scale;
@@ -928,7 +956,7 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   p.err = device_error_ptr();
   {
     dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)(a->B * a->H));
-    if (int rc = launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, tdo, tdq, p,
+    if (int rc = launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, tdo, tdq, tdk, tdv, p,
                             (const float2*)lsed, sq_pad))
       return rc;
   }

@@ -53,12 +53,21 @@ class LoRAInt8Linear(nn.Module):
         self.lora_up = nn.Parameter((torch.randn(out_f, rank, generator=generator, device=gdev) * 0.02).to(dtype).to(device))
         self.scale = alpha / rank
 
-    def forward(self, x):
+    def forward(self, x, h=None):
+        """`h`: this module's down-projection x A^T when the caller computed it (lora_down_shared)."""
         y = self.base(x)
-        h = F.linear(x, self.lora_down)
+        if h is None:
+            h = F.linear(x, self.lora_down)
         # the up-projection accumulates onto the base output in one GEMM: y + (h B^T) * alpha / r
         out = torch.addmm(y.reshape(-1, y.shape[-1]), h.reshape(-1, h.shape[-1]), self.lora_up.t(), alpha=self.scale)
         return out.view(y.shape)
+
+
+def lora_down_shared(x, mods):
+    """x A_i^T for LoRA modules that read the same input, as one GEMM over the stacked A_i (one launch
+    forward and two backward instead of one and two per module); returns one [..., r] view per module."""
+    w = torch.cat([m.lora_down for m in mods], 0)
+    return F.linear(x, w).split([m.lora_down.shape[0] for m in mods], dim=-1)
 
 
 class DiTBlock(nn.Module):
@@ -77,9 +86,15 @@ class DiTBlock(nn.Module):
     def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op):
         B, S, _ = xq.shape
         Skv = xkv_k.shape[1]
-        q = qp(xq).view(B, S, self.heads, self.d).transpose(1, 2)
-        k = kp(xkv_k).view(B, Skv, self.heads, self.d).transpose(1, 2)
-        v = vp(xkv_v).view(B, Skv, self.heads, self.d).transpose(1, 2)
+        # projections that read the same input share one LoRA down-projection GEMM
+        if xq is xkv_k and xkv_k is xkv_v:
+            hq, hk, hv = lora_down_shared(xq, (qp, kp, vp))
+        else:
+            hq = None
+            hk, hv = lora_down_shared(xkv_k, (kp, vp)) if xkv_k is xkv_v else (None, None)
+        q = qp(xq, hq).view(B, S, self.heads, self.d).transpose(1, 2)
+        k = kp(xkv_k, hk).view(B, Skv, self.heads, self.d).transpose(1, 2)
+        v = vp(xkv_v, hv).view(B, Skv, self.heads, self.d).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v)
         return op(o.transpose(1, 2).reshape(B, S, self.h))
 
