@@ -210,8 +210,14 @@ typedef struct b2_int8_gemm_args {
   int64_t x_ld, out_ld;
   int32_t scale_layout;
   int32_t transpose_w;
+  /* optional fp32 scratch of b2_int8_gemm_workspace_bytes() bytes (16-byte aligned) that lets GEMMs
+   * with too few output tiles for the GPU split their reduction (partials summed, plus the bias, by a
+   * second kernel); NULL or too small: no split */
+  void* workspace;
+  int64_t workspace_bytes;
 } b2_int8_gemm_args;
 int b2_int8_gemm(const b2_int8_gemm_args* args, b2_stream_t stream);
+uint64_t b2_int8_gemm_workspace_bytes(const b2_int8_gemm_args* args);
 
 /* Fused scaled-dot-product attention (no mask, no dropout, not causal), D <= 128.
  * Replaces k_sdpa_fwd / k_sdpa_bwd (csrc/ops_attn.cpp:166-295; kernels attn.comp.in and

@@ -409,7 +409,27 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           const int64_t col0 = n0 + cc;
           if (col0 >= p.N) return;  // warp-uniform
           if constexpr (W == 32) {
-            if (p.c_tma && !p.partial) {
+            if (p.c_tma == 2) {
+              // fp32 split-K partial: two 32-row x 16-column boxes through the staging tile
+              const int32_t r0 = (int32_t)(m0 + ms * BM + q * 32);
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                if (lane == 0) tc::bulk_wait_read0();
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  *reinterpret_cast<uint4*>(stg + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                      make_uint4(r[16 * hh + 4 * j], r[16 * hh + 4 * j + 1], r[16 * hh + 4 * j + 2], r[16 * hh + 4 * j + 3]);
+                tc::fence_async_shared();
+                __syncwarp();
+                if (lane == 0) {
+                  tc::tma_store_3d(&tmC, stg, (int32_t)(col0 + 16 * hh), r0, t / total_tiles);
+                  tc::bulk_commit();
+                }
+              }
+              return;
+            }
+            if (p.c_tma == 1 && !p.partial) {
               // bias / alpha in registers, bf16 row into the swizzled staging tile, one TMA store
               // of the warp's 32 x 32 box (rows past M and columns past N are clipped by the store)
               // in place: r[j] holds the fp32 bits of alpha * acc + beta * bias
@@ -703,7 +723,35 @@ __global__ void __launch_bounds__(256) gemm_splitk_reduce(const float* __restric
                                                           const OutT* __restrict__ bias, int64_t bias_sm,
                                                           int64_t bias_sn, float alpha, float beta) {
   const int64_t total = M * N;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if ((N & 3) == 0) {
+    // four consecutive columns of one row per thread, the partial loads of four slices in flight at once
+    for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < total; i += stride * 4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      int s = 0;
+      for (; s + 4 <= ksplit; s += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float4*>(part + (int64_t)(s + u) * total + i);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc.x += v[u].x, acc.y += v[u].y, acc.z += v[u].z, acc.w += v[u].w;
+      }
+      for (; s < ksplit; ++s) {
+        const float4 v = *reinterpret_cast<const float4*>(part + (int64_t)s * total + i);
+        acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+      }
+      const int64_t m = i / N, n = i % N;
+      const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = alpha * a4[e];
+        if (bias) v += beta * to_f32(bias[m * bias_sm + (n + e) * bias_sn]);
+        c[m * c_sm + (n + e) * c_sn] = from_f32<OutT>(v);
+      }
+    }
+    return;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
     float acc = 0.f;
     for (int s = 0; s < ksplit; ++s) acc += part[(int64_t)s * total + i];
     const int64_t m = i / N, n = i % N;
@@ -760,7 +808,17 @@ TileChoice pick_tile(int64_t M, int64_t N, int64_t batch) {
 // split-K partials.
 void setup_cmap(CUtensorMap* tm, CUtensorMapDataType dt, TcParams& p) {
   p.c_tma = 0, p.c3d = 0;
-  if (p.ksplit > 1 || p.c_sn != 1 || ((uintptr_t)p.c & 15)) return;
+  if (p.ksplit > 1) {
+    // split-K: the map describes the fp32 partials [ksplit][M][N] instead (32-row x 16-column boxes)
+    if (p.batch != 1 || (p.N % 4) || ((uintptr_t)p.partial & 15)) return;
+    uint64_t dims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.ksplit};
+    uint64_t strides[2] = {(uint64_t)p.N * 4, (uint64_t)p.N * p.M * 4};
+    uint32_t box[3] = {16, 32, 1};
+    if (make_tmap(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.partial, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B))
+      p.c_tma = 2;
+    return;
+  }
+  if (p.c_sn != 1 || ((uintptr_t)p.c & 15)) return;
   if (p.M > 1 && (p.c_sm * 2) % 16) return;
   const bool b3 = p.batch > 1;
   if (b3 && (p.c_sb == 0 || (p.c_sb * 2) % 16)) return;
@@ -893,6 +951,60 @@ uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a) {
   return ks > 1 ? (uint64_t)ks * a->M * a->N * sizeof(float) : 0;
 }
 
+// int8 launch plan. The dequant work per FLOP is 1/(2*rows of the CTA tile), so two stacked M=128
+// UMMA tiles (256 rows) halve it; among the shapes the kernel supports, take the one with the best
+// wave-quantised SM utilisation, weighted by how well the dequant warps keep up. The 176-wide tile
+// (forward only: the transposed form dequantises 64-column chunks) puts M = 1024, N = 6144 on
+// 140 CTAs, one wave. GEMMs with too few 256x256 tiles to fill the GPU and a long reduction (K >= 4096:
+// the DiT block's fc2 forward and fc1 dX at M = 1024) split it instead when the caller gives a
+// workspace: each work item is a 256x256 tile over a K slice of >= 8 blocks whose fp32 partial is
+// TMA-stored and summed (with the bias) by gemm_splitk_reduce. With K = 2048 the partial traffic and
+// the second kernel cost more than the split gains (measured 30 -> 45 us at 1024x2048x2048).
+struct Int8Plan {
+  int bn, msub, ksplit, kps;
+};
+Int8Plan int8_plan(const b2_int8_gemm_args* a) {
+  struct Choice { int bn, msub; double eff; };
+  const Choice fwd_opts[] = {{256, 2, 1.15}, {176, 2, 1.08}, {128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const Choice dx_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
+  const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
+  const int64_t out_cols = a->transpose_w ? a->K : a->N;
+  const int64_t red = a->transpose_w ? a->N : a->K;
+  const int k_blocks = (int)((red + BK - 1) / BK);
+  static const int forced = [] {  // B2_INT8_TILE=<bn>x<msub> pins the tile (measurement sweeps)
+    const char* e = getenv("B2_INT8_TILE");
+    int bn = 0, ms = 0;
+    return (e && sscanf(e, "%dx%d", &bn, &ms) == 2) ? bn * 10 + ms : 0;
+  }();
+  Int8Plan best{0, 0, 1, k_blocks};
+  double best_score = -1.0;
+  const int nopts = a->transpose_w ? 4 : 6;
+  for (int i = 0; i < nopts; ++i) {
+    const Choice c = a->transpose_w ? dx_opts[i] : fwd_opts[i];
+    const int64_t tiles = ((a->M + 128 * c.msub - 1) / (128 * c.msub)) * ((out_cols + c.bn - 1) / c.bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    double score = (double)a->M * out_cols / ((double)waves * sms * 128 * c.msub * c.bn) * c.eff;
+    if (forced) score = (forced == c.bn * 10 + c.msub) ? 1e9 : -1.0;
+    if (score > best_score) best_score = score, best = Int8Plan{c.bn, c.msub, 1, k_blocks};
+  }
+  if (best.bn == 0) best = Int8Plan{128, 2, 1, k_blocks};
+  // split-K over 256x256 tiles
+  const int64_t tiles = ((a->M + 255) / 256) * ((out_cols + 255) / 256);
+  if (!forced && a->workspace_bytes > 0 && tiles * 2 <= sms && k_blocks >= 64) {
+    const int want = (int)std::min<int64_t>(sms / tiles, k_blocks / 8);
+    if (want >= 2) {
+      const int kps = (k_blocks + want - 1) / want;
+      const int ks = (k_blocks + kps - 1) / kps;
+      const int64_t units = tiles * ks;
+      const int64_t waves = (units + sms - 1) / sms;
+      const double score = (double)a->M * out_cols / ((double)waves * sms * 256 * 256) * ks * 1.15 * 0.8;
+      const uint64_t need = (uint64_t)ks * a->M * out_cols * sizeof(float);
+      if (score > best_score && (uint64_t)a->workspace_bytes >= need) best = Int8Plan{256, 2, ks, kps};
+    }
+  }
+  return best;
+}
+
 }  // namespace b2
 
 using namespace b2;
@@ -913,32 +1025,10 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
     return fail(B2_ERR_ARG, "int8_gemm: x and q must be 16-byte aligned, x_ld a multiple of 8 and K of 16");
   if (a->transpose_w && a->bias) return fail(B2_ERR_ARG, "int8_gemm: bias is only supported in the forward form");
   cudaStream_t st = (cudaStream_t)stream;
-  // Tile choice. The dequant work per FLOP is 1/(2*rows of the CTA tile), so two stacked M=128 UMMA
-  // tiles (256 rows) halve it; among the shapes the kernel supports, take the one with the best
-  // wave-quantised SM utilisation, weighted by how well the dequant warps keep up. The 176-wide tile
-  // (forward only: the transposed form dequantises 64-column chunks) puts M = 1024, N = 6144 on
-  // 140 CTAs, one wave.
-  struct Choice { int bn, msub; double eff; };
-  const Choice fwd_opts[] = {{256, 2, 1.15}, {176, 2, 1.08}, {128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
-  const Choice dx_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
-  const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
-  Choice best{0, 0, -1.0};
-  double best_score = -1.0;
-  const int nopts = a->transpose_w ? 4 : 6;
-  static const int forced = [] {  // B2_INT8_TILE=<bn>x<msub> pins the tile (measurement sweeps)
-    const char* e = getenv("B2_INT8_TILE");
-    int bn = 0, ms = 0;
-    return (e && sscanf(e, "%dx%d", &bn, &ms) == 2) ? bn * 10 + ms : 0;
-  }();
-  for (int i = 0; i < nopts; ++i) {
-    const Choice c = a->transpose_w ? dx_opts[i] : fwd_opts[i];
-    const int64_t tiles = ((a->M + 128 * c.msub - 1) / (128 * c.msub)) * ((out_cols + c.bn - 1) / c.bn);
-    const int64_t waves = (tiles + sms - 1) / sms;
-    double score = (double)a->M * out_cols / ((double)waves * sms * 128 * c.msub * c.bn) * c.eff;
-    if (forced) score = (forced == c.bn * 10 + c.msub) ? 1e9 : -1.0;
-    if (score > best_score) best_score = score, best = c;
-  }
-  if (best.bn == 0) best = a->transpose_w ? dx_opts[1] : fwd_opts[1];
+  if (a->workspace && ((uintptr_t)a->workspace & 15)) return fail(B2_ERR_ARG, "int8_gemm: workspace must be 16-byte aligned");
+  b2_int8_gemm_args aa = *a;
+  if (!aa.workspace) aa.workspace_bytes = 0;
+  const Int8Plan best = int8_plan(&aa);
   const int BN = best.bn, BMT = 128 * best.msub;
   TcParams p{};
   p.M = a->M, p.N = out_cols, p.K = red, p.batch = 1;
@@ -952,7 +1042,8 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   p.alpha = 1.f, p.beta = 1.f;
   p.err = device_error_ptr();
   p.scale = a->scale, p.scale_layout = a->scale_layout, p.scale_nb = (a->K + 63) / 64, p.deq_rows = a->N;
-  p.ksplit = 1, p.kps = p.k_blocks;
+  p.ksplit = best.ksplit, p.kps = best.kps;
+  if (p.ksplit > 1) p.partial = (float*)a->workspace;
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   setup_cmap(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p);
@@ -972,10 +1063,27 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
       return fail(B2_ERR_ARG, "int8_gemm: tensor map for q rejected");
   }
   const char* name = a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd";
-  if (best.msub == 2 && BN == 256) return launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name);
-  if (best.msub == 2 && BN == 176) return launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name);
-  if (best.msub == 2 && BN == 128) return launch_kernel<128, true, 2, 2>(ta, tb, tcm, p, st, name);
-  if (best.msub == 2 && BN == 96) return launch_kernel<96, true, 2, 2>(ta, tb, tcm, p, st, name);
-  if (BN == 256) return launch_kernel<256, true, 2, 1>(ta, tb, tcm, p, st, name);
-  return launch_kernel<128, true, 2, 1>(ta, tb, tcm, p, st, name);
+  int rc;
+  if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name);
+  else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name);
+  else if (best.msub == 2 && BN == 128) rc = launch_kernel<128, true, 2, 2>(ta, tb, tcm, p, st, name);
+  else if (best.msub == 2 && BN == 96) rc = launch_kernel<96, true, 2, 2>(ta, tb, tcm, p, st, name);
+  else if (BN == 256) rc = launch_kernel<256, true, 2, 1>(ta, tb, tcm, p, st, name);
+  else rc = launch_kernel<128, true, 2, 1>(ta, tb, tcm, p, st, name);
+  if (rc || p.ksplit == 1) return rc;
+  const int64_t total = a->M * out_cols;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)device_info().sm_count * 8);
+  LaunchScope ls("int8_gemm_splitk_reduce", st);
+  gemm_splitk_reduce<__nv_bfloat16><<<grid, 256, 0, st>>>(p.partial, p.ksplit, a->M, out_cols, (__nv_bfloat16*)a->out,
+                                                          a->out_ld, 1, (const __nv_bfloat16*)a->bias, 0, 1, 1.f, 1.f);
+  return after_launch("int8_gemm_splitk_reduce");
+}
+
+extern "C" uint64_t b2_int8_gemm_workspace_bytes(const b2_int8_gemm_args* a) {
+  if (!a || a->M <= 0 || a->N <= 0 || a->K <= 0 || !device_info().tcgen05) return 0;
+  b2_int8_gemm_args q = *a;
+  q.workspace = nullptr, q.workspace_bytes = INT64_MAX;  // the plan a large enough workspace gets
+  const Int8Plan pl = int8_plan(&q);
+  const int64_t out_cols = a->transpose_w ? a->K : a->N;
+  return pl.ksplit > 1 ? (uint64_t)pl.ksplit * a->M * out_cols * sizeof(float) : 0;
 }

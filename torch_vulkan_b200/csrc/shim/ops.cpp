@@ -617,6 +617,17 @@ at::Tensor b2_dequant_int8_op(const at::Tensor& q0, const at::Tensor& scale0, at
   return out;
 }
 
+// split-K scratch for the int8 GEMM (GEMMs with too few output tiles to fill the GPU) from the
+// caching allocator; the returned tensor keeps it alive for the call
+at::Tensor int8_workspace(b2_int8_gemm_args& g, const at::Tensor& like) {
+  at::Tensor ws;
+  if (const uint64_t wsb = b2_int8_gemm_workspace_bytes(&g)) {
+    ws = at::empty({(int64_t)wsb}, like.options().dtype(at::kByte));
+    g.workspace = ws.data_ptr(), g.workspace_bytes = (int64_t)wsb;
+  }
+  return ws;
+}
+
 // y[..., N] = x[..., K] @ (q * scale)^T + bias
 at::Tensor b2_int8_linear_fwd(const at::Tensor& x0, const at::Tensor& q, const at::Tensor& scale0,
                               const std::optional<at::Tensor>& bias0) {
@@ -646,6 +657,7 @@ at::Tensor b2_int8_linear_fwd(const at::Tensor& x0, const at::Tensor& q, const a
   g.M = x.size(0), g.N = N, g.K = K, g.x_ld = K, g.out_ld = N;
   g.scale_layout = layout;
   g.transpose_w = 0;
+  at::Tensor ws = int8_workspace(g, x);
   b2_check(b2_int8_gemm(&g, cur_stream()), "int8_linear_fwd");
   count("b2::int8_linear");
   return out.view(osz);
@@ -670,6 +682,7 @@ at::Tensor b2_int8_linear_dx(const at::Tensor& dy0, const at::Tensor& q, const a
   g.M = dy.size(0), g.N = N, g.K = K, g.x_ld = N, g.out_ld = K;
   g.scale_layout = layout;
   g.transpose_w = 1;
+  at::Tensor ws = int8_workspace(g, dy);
   b2_check(b2_int8_gemm(&g, cur_stream()), "int8_linear_dx");
   count("b2::int8_linear_dx");
   return dx.view(osz);
