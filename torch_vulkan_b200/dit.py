@@ -53,9 +53,11 @@ class LoRAInt8Linear(nn.Module):
         self.lora_up = nn.Parameter((torch.randn(out_f, rank, generator=generator, device=gdev) * 0.02).to(dtype).to(device))
         self.scale = alpha / rank
 
-    def forward(self, x, h=None):
-        """`h`: this module's down-projection x A^T when the caller computed it (lora_down_shared)."""
-        y = self.base(x)
+    def forward(self, x, h=None, y=None):
+        """`h`: this module's down-projection x A^T, `y`: its base output, when the caller computed them
+        (lora_down_shared; a stacked int8 GEMM over several modules' base weights)."""
+        if y is None:
+            y = self.base(x)
         if h is None:
             h = F.linear(x, self.lora_down)
         # the up-projection accumulates onto the base output in one GEMM: y + (h B^T) * alpha / r
@@ -82,19 +84,40 @@ class DiTBlock(nn.Module):
         self.fc2 = Int8Linear(mlp, hidden, generator=g, device=device)
         # adaLN modulation: (shift, scale, gate) for self-attn, cross-attn and MLP from the conditioning vector
         self.ada = Int8Linear(hidden, 9 * hidden, generator=g, device=device)
+        # projections that read the same input keep their frozen int8 bases in one stacked weight
+        # (each module's base buffers are views of it): one GEMM forward and one dX GEMM backward
+        self._stack_bases("qkv", (self.q, self.k, self.v))
+        self._stack_bases("ckv", (self.ck, self.cv))
+
+    def _stack_bases(self, name, mods):
+        for part in ("q", "scale", "bias"):
+            full = torch.cat([getattr(m.base, part) for m in mods], 0)
+            self.register_buffer(f"{name}_{part}", full)
+            o = 0
+            for m in mods:
+                n = getattr(m.base, part).shape[0]
+                setattr(m.base, part, full[o:o + n])
+                o += n
+
+    def _stacked(self, name, x, mods):
+        y = tv.int8_linear(x, getattr(self, f"{name}_q"), getattr(self, f"{name}_scale"), getattr(self, f"{name}_bias"))
+        return y.split([m.base.q.shape[0] for m in mods], dim=-1)
 
     def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op):
         B, S, _ = xq.shape
         Skv = xkv_k.shape[1]
-        # projections that read the same input share one LoRA down-projection GEMM
-        if xq is xkv_k and xkv_k is xkv_v:
+        # projections that read the same input share one stacked int8 GEMM and one LoRA
+        # down-projection GEMM
+        hq = hk = hv = yq = yk = yv = None
+        if xq is xkv_k and xkv_k is xkv_v and qp is self.q:
             hq, hk, hv = lora_down_shared(xq, (qp, kp, vp))
-        else:
-            hq = None
-            hk, hv = lora_down_shared(xkv_k, (kp, vp)) if xkv_k is xkv_v else (None, None)
-        q = qp(xq, hq).view(B, S, self.heads, self.d).transpose(1, 2)
-        k = kp(xkv_k, hk).view(B, Skv, self.heads, self.d).transpose(1, 2)
-        v = vp(xkv_v, hv).view(B, Skv, self.heads, self.d).transpose(1, 2)
+            yq, yk, yv = self._stacked("qkv", xq, (qp, kp, vp))
+        elif xkv_k is xkv_v and kp is self.ck:
+            hk, hv = lora_down_shared(xkv_k, (kp, vp))
+            yk, yv = self._stacked("ckv", xkv_k, (kp, vp))
+        q = qp(xq, hq, yq).view(B, S, self.heads, self.d).transpose(1, 2)
+        k = kp(xkv_k, hk, yk).view(B, Skv, self.heads, self.d).transpose(1, 2)
+        v = vp(xkv_v, hv, yv).view(B, Skv, self.heads, self.d).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v)
         return op(o.transpose(1, 2).reshape(B, S, self.h))
 
