@@ -53,23 +53,26 @@ class LoRAInt8Linear(nn.Module):
         self.lora_up = nn.Parameter((torch.randn(out_f, rank, generator=generator, device=gdev) * 0.02).to(dtype).to(device))
         self.scale = alpha / rank
 
-    def forward(self, x, h=None, y=None):
-        """`h`: this module's down-projection x A^T, `y`: its base output, when the caller computed them
-        (lora_down_shared; a stacked int8 GEMM over several modules' base weights)."""
-        if y is None:
-            y = self.base(x)
-        if h is None:
-            h = F.linear(x, self.lora_down)
+    def forward(self, x):
+        y = self.base(x)
+        h = F.linear(x, self.lora_down)
         # the up-projection accumulates onto the base output in one GEMM: y + (h B^T) * alpha / r
         out = torch.addmm(y.reshape(-1, y.shape[-1]), h.reshape(-1, h.shape[-1]), self.lora_up.t(), alpha=self.scale)
         return out.view(y.shape)
 
 
-def lora_down_shared(x, mods):
-    """x A_i^T for LoRA modules that read the same input, as one GEMM over the stacked A_i (one launch
-    forward and two backward instead of one and two per module); returns one [..., r] view per module."""
-    w = torch.cat([m.lora_down for m in mods], 0)
-    return F.linear(x, w).split([m.lora_down.shape[0] for m in mods], dim=-1)
+def stacked_lora_forward(x, q, scale, bias, mods):
+    """LoRAInt8Linear.forward of several modules that read the same input x, with their frozen int8
+    bases stacked in (q, scale, bias): one int8 GEMM, one down-projection GEMM over the stacked A_i and
+    one up-projection GEMM over the block-diagonal B_i accumulated onto the base output (backward: one
+    dX GEMM, and one GEMM each for dh, dA and dB, instead of one of each per module). Returns one
+    [..., out_i] view per module."""
+    y = tv.int8_linear(x, q, scale, bias)
+    h = F.linear(x, torch.cat([m.lora_down for m in mods], 0))
+    bd = torch.block_diag(*[m.lora_up for m in mods])
+    n = y.shape[-1]
+    out = torch.addmm(y.reshape(-1, n), h.reshape(-1, h.shape[-1]), bd.t(), alpha=mods[0].scale)
+    return out.view(y.shape).split([m.base.q.shape[0] for m in mods], dim=-1)
 
 
 class DiTBlock(nn.Module):
@@ -100,24 +103,24 @@ class DiTBlock(nn.Module):
                 o += n
 
     def _stacked(self, name, x, mods):
-        y = tv.int8_linear(x, getattr(self, f"{name}_q"), getattr(self, f"{name}_scale"), getattr(self, f"{name}_bias"))
-        return y.split([m.base.q.shape[0] for m in mods], dim=-1)
+        assert all(m.scale == mods[0].scale for m in mods)
+        return stacked_lora_forward(x, getattr(self, f"{name}_q"), getattr(self, f"{name}_scale"),
+                                    getattr(self, f"{name}_bias"), mods)
 
     def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op):
         B, S, _ = xq.shape
         Skv = xkv_k.shape[1]
-        # projections that read the same input share one stacked int8 GEMM and one LoRA
-        # down-projection GEMM
-        hq = hk = hv = yq = yk = yv = None
+        # projections that read the same input run as one stacked group (stacked_lora_forward)
         if xq is xkv_k and xkv_k is xkv_v and qp is self.q:
-            hq, hk, hv = lora_down_shared(xq, (qp, kp, vp))
-            yq, yk, yv = self._stacked("qkv", xq, (qp, kp, vp))
+            q, k, v = self._stacked("qkv", xq, (qp, kp, vp))
         elif xkv_k is xkv_v and kp is self.ck:
-            hk, hv = lora_down_shared(xkv_k, (kp, vp))
-            yk, yv = self._stacked("ckv", xkv_k, (kp, vp))
-        q = qp(xq, hq, yq).view(B, S, self.heads, self.d).transpose(1, 2)
-        k = kp(xkv_k, hk, yk).view(B, Skv, self.heads, self.d).transpose(1, 2)
-        v = vp(xkv_v, hv, yv).view(B, Skv, self.heads, self.d).transpose(1, 2)
+            q = qp(xq)
+            k, v = self._stacked("ckv", xkv_k, (kp, vp))
+        else:
+            q, k, v = qp(xq), kp(xkv_k), vp(xkv_v)
+        q = q.view(B, S, self.heads, self.d).transpose(1, 2)
+        k = k.view(B, Skv, self.heads, self.d).transpose(1, 2)
+        v = v.view(B, Skv, self.heads, self.d).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v)
         return op(o.transpose(1, 2).reshape(B, S, self.h))
 
