@@ -586,6 +586,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     int gk = 0;  // K blocks dequantised so far (B ring position)
     constexpr int FIPT = (BN * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
     float fsc[FIPT];
+    constexpr int IPT = (64 * (BN / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // transposed items per thread
+    float sc[IPT];
     for (int t = blockIdx.x; t < total_work; t += gridDim.x) {
       int m0, n0, b, kb0, kb1;
       tile_coords(t, m0, n0, b);
@@ -607,6 +609,21 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
         }
         const int rs = gk % NR;
+        if (p.b_mn) {
+          // transposed form: the scale of reduction row nf = kb * 64 + i, loaded before the waits
+#pragma unroll
+          for (int u = 0; u < IPT; ++u) {  // every scale load in flight before the first is used
+            const int e = dt + u * NDQ;
+            const int i = e / (BN / 16), qd = e % (BN / 16);
+            const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
+            const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
+            sc[u] = 0.f;
+            if (e < 64 * (BN / 16) && nf < p.deq_rows)
+              sc[u] = p.scale_layout == 0
+                          ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
+                          : reinterpret_cast<const float*>(p.scale)[nf];
+          }
+        }
         if (!tc::mbar_wait(&rfull[rs], (uint32_t)((gk / NR) & 1), p.err) || *abort_flag) {
           ok = false;
           break;
@@ -638,20 +655,6 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         } else {
           // backward: raw [64 rows i (n_feat)][BN bytes (k_feat = n_gemm)]; B stage MN-major SW128:
           // chunk j = n_gemm/64 at j*8192, row i at i*128, 16 B granule g at ((g ^ (i & 7)) * 16).
-          constexpr int IPT = (64 * (BN / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // items per thread
-          float sc[IPT];
-#pragma unroll
-          for (int u = 0; u < IPT; ++u) {  // every scale load in flight before the first is used
-            const int e = dt + u * NDQ;
-            const int i = e / (BN / 16), qd = e % (BN / 16);
-            const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
-            const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
-            sc[u] = 0.f;
-            if (e < 64 * (BN / 16) && nf < p.deq_rows)
-              sc[u] = p.scale_layout == 0
-                          ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
-                          : reinterpret_cast<const float*>(p.scale)[nf];
-          }
 #pragma unroll
           for (int u = 0; u < IPT; ++u) {
             const int e = dt + u * NDQ;
