@@ -166,13 +166,28 @@ __global__ void __launch_bounds__(256) softmax_fwd_reg(const TI* __restrict__ x,
 }
 
 template <typename TI, typename TO, int GROUP, int V, int NCH>
-__global__ void __launch_bounds__(256, 3) softmax_bwd_reg(const TI* __restrict__ yv, const TI* __restrict__ g,
+__global__ void __launch_bounds__(256, 2) softmax_bwd_reg(const TI* __restrict__ yv, const TI* __restrict__ g,
                                                        TO* __restrict__ dx, int64_t rows, int64_t R) {
+  // persistent row groups (two blocks per SM): the next row's y and g are loaded, and stay in flight,
+  // while the current row is reduced and written
   __shared__ float red[32];
   const int rpb = blockDim.x / GROUP;
   const int t = threadIdx.x % GROUP;
-  for (int64_t row = (int64_t)blockIdx.x * rpb + threadIdx.x / GROUP; row - threadIdx.x / GROUP < rows;
-       row += (int64_t)gridDim.x * rpb) {
+  const int64_t stride = (int64_t)gridDim.x * rpb;
+  RawVec<TI, V> ny[NCH], ng[NCH];
+  int64_t row = (int64_t)blockIdx.x * rpb + threadIdx.x / GROUP;
+  auto fetch = [&](int64_t r) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t idx = ((int64_t)c * GROUP + t) * V;
+      if (r < rows && idx < R) {
+        ny[c].load(yv + r * R + idx);
+        ng[c].load(g + r * R + idx);
+      }
+    }
+  };
+  fetch(row);
+  for (; row - threadIdx.x / GROUP < rows; row += stride) {
     const bool active = row < rows;
     float a[NCH][V], b[NCH][V];
     float d = 0.f;
@@ -180,12 +195,13 @@ __global__ void __launch_bounds__(256, 3) softmax_bwd_reg(const TI* __restrict__
     for (int c = 0; c < NCH; ++c) {
       int64_t idx = ((int64_t)c * GROUP + t) * V;
       if (active && idx < R) {
-        VecIO<TI, V>::load(yv + row * R + idx, a[c]);
-        VecIO<TI, V>::load(g + row * R + idx, b[c]);
+        ny[c].get(a[c]);
+        ng[c].get(b[c]);
 #pragma unroll
         for (int i = 0; i < V; ++i) d += a[c][i] * b[c][i];
       }
     }
+    fetch(row + stride);
     d = group_sum<GROUP>(d, red);
     if (!active) continue;
 #pragma unroll
@@ -292,7 +308,10 @@ template <typename TI, typename TO, int GROUP, int V, int NCH>
 void launch_softmax_reg(const b2_softmax_args* a, cudaStream_t st, bool fwd) {
   const int threads = 256;
   const int rpb = threads / GROUP;
-  int grid = grid_for((a->outer + rpb - 1) / rpb, 1, 16);
+  // backward: persistent row groups with the next row prefetched; rows of 4+ vectors per lane keep
+  // enough bytes in flight at two blocks per SM, shorter rows need more resident blocks
+  const int bwd_per_sm = NCH * V * (int)sizeof(TI) >= 64 ? 2 : (NCH * V * (int)sizeof(TI) >= 32 ? 4 : 8);
+  int grid = grid_for((a->outer + rpb - 1) / rpb, 1, fwd ? 16 : bwd_per_sm);
   if (fwd)
     softmax_fwd_reg<TI, TO, GROUP, V, NCH><<<grid, threads, 0, st>>>((const TI*)a->x, (TO*)a->out, a->outer, a->R, a->safe);
   else
@@ -551,13 +570,15 @@ __global__ void __launch_bounds__(256) ln_bwd_reg(const T* __restrict__ x, const
 }
 
 // Column sum of the partials: dw[d] = sum_s part[s][d], db[d] = sum_s part[s][D + d].
-// blockDim = (32, 32): x over 32 consecutive columns (128-byte loads per slot), y over the slots;
-// the 32 slot lanes are combined through shared memory.
+// blockDim = (8, 32): x over 8 consecutive columns (32-byte sectors per slot), y over the slots; 8
+// columns per block spread the partials (L2-resident: the backward kernel just wrote them) over
+// D / 8 blocks, and the 32 slot lanes are combined through shared memory.
+constexpr int kWgradCols = 8;
 template <typename T>
-__global__ void __launch_bounds__(1024) ln_wgrad_reduce(const float* __restrict__ part, int64_t nslots, int64_t D,
-                                                        T* __restrict__ dw, T* __restrict__ db) {
-  __shared__ float sw[32][33], sb[32][33];
-  const int64_t col = (int64_t)blockIdx.x * 32 + threadIdx.x;
+__global__ void __launch_bounds__(256) ln_wgrad_reduce(const float* __restrict__ part, int64_t nslots, int64_t D,
+                                                       T* __restrict__ dw, T* __restrict__ db) {
+  __shared__ float sw[32][kWgradCols + 1], sb[32][kWgradCols + 1];
+  const int64_t col = (int64_t)blockIdx.x * kWgradCols + threadIdx.x;
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the partials of the preceding backward kernel
   float aw0 = 0.f, ab0 = 0.f, aw1 = 0.f, ab1 = 0.f;
   if (col < D) {
@@ -780,7 +801,8 @@ int ln_run(const b2_layernorm_args* a, cudaStream_t st, bool fwd) {
     }
   }
   if (want_w) {
-    if (int rc = launch_pdl("layernorm_wgrad_reduce", ln_wgrad_reduce<T>, dim3((unsigned)((a->D + 31) / 32)), dim3(32, 32),
+    if (int rc = launch_pdl("layernorm_wgrad_reduce", ln_wgrad_reduce<T>,
+                            dim3((unsigned)((a->D + kWgradCols - 1) / kWgradCols)), dim3(kWgradCols, 32),
                             0, st, (const float*)part, p.nslots, a->D, (T*)a->dw, (T*)a->db))
       return rc;
   }
@@ -860,8 +882,9 @@ int ln_bwd_planned(const b2_layernorm_args* a, const LnPlan& p, float* part, cud
   }
   if (want_w) {
     LaunchScope ls("layernorm_wgrad_reduce_noalloc", st);
-    dim3 block(32, 32);
-    ln_wgrad_reduce<T><<<(unsigned)((a->D + 31) / 32), block, 0, st>>>(pw, p.nslots, a->D, (T*)a->dw, (T*)a->db);
+    dim3 block(kWgradCols, 32);
+    ln_wgrad_reduce<T><<<(unsigned)((a->D + kWgradCols - 1) / kWgradCols), block, 0, st>>>(pw, p.nslots, a->D, (T*)a->dw,
+                                                                                             (T*)a->db);
   }
   return after_launch("b2_layernorm_bwd_noalloc");
 }
