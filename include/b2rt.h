@@ -72,6 +72,14 @@ int b2rt_sm_count(void);
 /* Device-side error word written by kernels whose bounded waits expired (0 = none).
  * reset != 0 clears it. Synchronises the device. */
 int b2rt_device_error(int reset);
+/* Replaces vkrt_validation_errors (vkrt.h:28, lib.rs:1183-1186): the number of launches this
+ * library's runtime refused, plus 1 when the device error word is set. It does not synchronise the
+ * device: the word is read by a copy on a private stream, so a kernel still in flight may set it
+ * after the read (b2rt_device_error waits for everything). */
+size_t b2rt_validation_errors(void);
+/* Replaces vkrt_coop_caps (vkrt.h:31, lib.rs:1242-1244): bit 0 = f16 and bit 1 = bf16 tensor-core
+ * GEMM available (a tcgen05-capable sm_100a device is current); 0 without one. */
+uint32_t b2rt_coop_caps(void);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Memory: slab sub-allocator (replaces vkrt/src/lib.rs:646-810 and the c10 allocator at       */
@@ -102,7 +110,11 @@ size_t b2rt_slab_count(void);                       /* vkrt_slab_count (lib.rs:1
 int b2rt_debug_host_backend(int on);
 
 /* torch.cuda.memory.CUDAPluggableAllocator entry points (same slab allocator, stream-aware:
- * a block freed on stream S is reused on another stream only after that stream waits on S). */
+ * a block freed on stream S is reused on another stream only after that stream waits on S).
+ * Each device ordinal has its own slabs: b2_malloc/b2_free use `device`; the b2rt_* memory calls
+ * above act on the calling thread's current device, except b2rt_free, b2rt_upload, b2rt_download
+ * and b2rt_copy_d2d, which find the device that owns the address. The memory limit applies to
+ * every device separately. */
 void* b2_malloc(ptrdiff_t size, int device, b2_stream_t stream);
 void b2_free(void* ptr, ptrdiff_t size, int device, b2_stream_t stream);
 
@@ -302,7 +314,9 @@ uint64_t b2_layernorm_bwd_workspace_bytes(const b2_layernorm_args* args);
  * 2 MiB scratch array compiled into the library (kept by every GPU that loads it until exit), so
  * D <= 262144 when dw or db is requested; larger D is rejected with B2_ERR_ARG. The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress), so make it before any CUDA
- * graph capture. Every call reuses the same array: calls that can overlap on the GPU (different
+ * graph capture. The address is cached per device for the life of the process and is not valid after
+ * cudaDeviceReset (or anything else that destroys the device's primary context): do not call this entry
+ * point after such a reset. Every call reuses the same array: calls that can overlap on the GPU (different
  * streams, no ordering between them) race; calls ordered on one stream are safe. Nothing in the
  * array needs to start at zero (every partial is written before it is read). */
 int b2_layernorm_bwd_noalloc(const b2_layernorm_args* args, b2_stream_t stream);

@@ -1,8 +1,9 @@
 """Generates the golden fixtures in this directory by running the REFERENCE's own Python code.
 
-Run only where the reference sources are present (default path below, or $B2_REFERENCE_ROOT):
+Run only where the reference sources are present; give their root as the argument or in
+$B2_REFERENCE_ROOT:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference-root>
 
 The reference package cannot be imported as a whole here (``import torch_vulkan`` dlopens its Vulkan
 extension, torch_vulkan/__init__.py:18-29), so this script parses the reference files with ``ast`` and
@@ -34,7 +35,9 @@ import torch
 import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("B2_REFERENCE_ROOT", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("B2_REFERENCE_ROOT", "")
+if not REF or not os.path.isdir(REF):
+    sys.exit("make_golden.py: pass the reference source root as the argument or set B2_REFERENCE_ROOT")
 
 
 def load_functions(path, names, extra_globals=None):

@@ -34,13 +34,23 @@ def run_dev(q, k, v, g):
     return o.detach().cpu(), qv.grad.cpu(), kv.grad.cpu(), vv.grad.cpu()
 
 
+def dev_lse(q, k, v):
+    """logsumexp [B,H,Sq] fp32 as the fused forward returns it (the op F.scaled_dot_product_attention reaches)."""
+    return torch.ops.aten._scaled_dot_product_fused_attention_overrideable(q.cuda(), k.cuda(), v.cuda())[1].cpu()
+
+
 def check_all(q, k, v, g, dtype, got):
-    o64, _ = oracle.sdpa_fwd(q, k, v)
+    o64, lse64 = oracle.sdpa_fwd(q, k, v)
     dq64, dk64, dv64 = oracle.sdpa_bwd(q, k, v, g)
     for name, x, ref in zip(("out", "dq", "dk", "dv"), got, (o64, dq64, dk64, dv64)):
         assert x.dtype == dtype and x.shape == ref.shape, name
         e = rel_err(x, ref)
         assert e < ATTN_REL[dtype], f"{name}: rel err {e}"
+    # logsumexp is an fp32 statistic: 1e-3 relative (of max(1, |lse|)) whatever the input dtype
+    lse = dev_lse(q, k, v)
+    assert lse.dtype == torch.float32 and lse.shape == lse64.shape
+    err = (lse.double() - lse64).abs().max().item()
+    assert err <= 1e-3 * max(1.0, lse64.abs().max().item()), f"lse: max err {err}"
 
 
 @pytest.mark.parametrize("dtype", DTYPES)

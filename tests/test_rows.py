@@ -121,8 +121,34 @@ def test_layer_norm_backward(tv, dt, affine, rows, D):
     F.layer_norm(xd, (D,), wd, bd, 1e-5).backward(g.cuda())
     row_close(xd.grad, dx64, dt, mult=4.0)
     if affine:
-        # column sums over `rows` terms: scale the tolerance like a K-long reduction
-        mult = 4.0 * (1 + 0.05 * rows ** 0.5)
-        row_close(wd.grad, dw64, dt, mult=mult)
-        row_close(bd.grad, db64, dt, mult=mult)
+        # dw, db: 2e-2 of max|ref| in bf16 (the gradient tolerance of the hot path), 3e-5 in fp32
+        rel_close(wd.grad, dw64, 2e-2 if dt == torch.bfloat16 else 3e-5)
+        rel_close(bd.grad, db64, 2e-2 if dt == torch.bfloat16 else 3e-5)
     assert tv.kernel_counts().get("aten::native_layer_norm_backward", 0) == 1
+
+
+def rel_close(out, ref64, rtol):
+    o, r = out.detach().cpu().double(), ref64.double()
+    assert o.shape == r.shape
+    err = (o - r).abs().max().item()
+    assert err <= rtol * r.abs().max().item(), f"max err {err} (max|ref| {r.abs().max().item()})"
+
+
+def test_layer_norm_config3():
+    """BASELINE configs[2] LayerNorm: bf16 [1024, 2048] ~N(0,1), w ~N(1,0.1), b ~N(0,0.1), eps 1e-6, grad ~N(0,1).
+    y within bf16 tolerance, fp32 mean/rstd within 1e-3 relative, dx/dw/db within 2e-2 of max|ref|."""
+    x = rnd_normal((1024, 2048), torch.bfloat16, seed=0)
+    w = (1 + rnd_normal((2048,), seed=1, scale=0.1)).to(torch.bfloat16)
+    b = rnd_normal((2048,), torch.bfloat16, seed=2, scale=0.1)
+    g = rnd_normal((1024, 2048), torch.bfloat16, seed=3)
+    xd, wd, bd = (t.cuda().requires_grad_(True) for t in (x, w, b))
+    y, mean, rstd = torch.native_layer_norm(xd, (2048,), wd, bd, 1e-6)
+    y64, m64, r64 = oracle.layer_norm(x, (2048,), w, b, eps=1e-6)
+    row_close(y, y64, torch.bfloat16, mult=2.0)
+    assert torch.allclose(mean.detach().cpu().double(), m64, rtol=1e-3, atol=1e-6)
+    assert torch.allclose(rstd.detach().cpu().double(), r64, rtol=1e-3)
+    y.backward(g.cuda())
+    dx64, dw64, db64 = oracle.layer_norm_bwd(x, g, (2048,), w, 1e-6)
+    rel_close(xd.grad, dx64, 2e-2)
+    rel_close(wd.grad, dw64, 2e-2)
+    rel_close(bd.grad, db64, 2e-2)

@@ -77,6 +77,25 @@ def test_noalloc_layernorm_backward_matches_regular_entry(dt, rows, D):
             assert torch.allclose(a.float(), b.float(), **tol), (name, (a.float() - b.float()).abs().max().item())
 
 
+def test_noalloc_long_rows_use_fewer_partial_slots():
+    """fp32 rows of 100000 elements take the long-row kernels; the 2 MiB scratch holds only two partial
+    slots of 2 x 100000 floats (the regular entry plans far more), so each slot sums 300 of the 600 rows."""
+    L = lib()
+    rows, D = 600, 100_000
+    gen = torch.Generator().manual_seed(rows + D)
+    x = torch.randn(rows, D, generator=gen).cuda()
+    w = (1 + 0.1 * torch.randn(D, generator=gen)).cuda()
+    g = torch.randn(rows, D, generator=gen).cuda()
+    _, mean, rstd = torch.native_layer_norm(x, (D,), w, None, 1e-6)
+    mean, rstd = mean.reshape(rows).contiguous(), rstd.reshape(rows).contiguous()
+    ref = run_once(L, x, w, g, mean, rstd, noalloc=False)
+    for _ in range(2):
+        got = run_once(L, x, w, g, mean, rstd, noalloc=True)
+        assert torch.equal(got[0], ref[0])
+        for name, a, b in (("dw", got[1], ref[1]), ("db", got[2], ref[2])):
+            assert torch.allclose(a, b, rtol=1e-5, atol=1e-4), (name, (a - b).abs().max().item())
+
+
 def test_noalloc_rejects_rows_wider_than_the_scratch():
     L = lib()
     D = 300_000  # 2 * D floats > the 512 Ki-float scratch

@@ -59,6 +59,8 @@ _lib.b2rt_op_counts.restype = ctypes.c_size_t
 _lib.b2rt_profile_dump.restype = ctypes.c_size_t
 _lib.b2rt_last_error.restype = ctypes.c_size_t
 _lib.b2rt_device_name.restype = ctypes.c_size_t
+_lib.b2rt_validation_errors.restype = ctypes.c_size_t
+_lib.b2rt_coop_caps.restype = ctypes.c_uint32
 
 _STAT_NAMES = ["launches", "launch_ns", "upload_bytes", "download_bytes", "allocs", "frees", "sync_ns",
                "cross_stream_waits"]
@@ -251,8 +253,8 @@ def set_tc_attention_enabled(on: bool) -> None:
 
 
 def coop_caps() -> int:
-    """bit0 = f16, bit1 = bf16 tensor-core GEMM available (sm_100a device present)."""
-    return 3 if torch.cuda.is_available() and torch.cuda.get_device_capability() == (10, 0) else 0
+    """bit0 = f16, bit1 = bf16 tensor-core GEMM available (a tcgen05-capable sm_100a device is current)."""
+    return int(_lib.b2rt_coop_caps()) if torch.cuda.is_available() else 0
 
 
 def gemm_path(a: torch.Tensor, b: torch.Tensor) -> str:

@@ -14,7 +14,11 @@
 //   * stream awareness for the PyTorch pluggable-allocator entry points: a free range remembers the
 //     streams that freed into it; a carve for stream T makes T wait (cudaStreamWaitEvent, no host
 //     sync) on each other stream S recorded there, so a block is never reused across streams before
-//     the work that used it is ordered ahead.
+//     the work that used it is ordered ahead;
+//   * one allocator per device ordinal (the reference runtime drives a single Vulkan device): slabs,
+//     free ranges and statistics never mix devices. b2_malloc/b2_free use their device argument; the
+//     b2rt_* calls without one use the calling thread's current CUDA device, and b2rt_free and the
+//     copy calls find the device that owns the address.
 #include <cuda_runtime.h>
 #include <stdlib.h>
 #include <string.h>
@@ -58,8 +62,27 @@ void merge_streams(std::vector<cudaStream_t>& into, const std::vector<cudaStream
     if (std::find(into.begin(), into.end(), s) == into.end()) into.push_back(s);
 }
 
+// Makes `dev` current for the lifetime of the guard (no-op when it already is).
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return;
+    }
+    if (cur != dev && cudaSetDevice(dev) == cudaSuccess) prev = cur;
+    (void)cudaGetLastError();
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
 class Allocator {
  public:
+  explicit Allocator(int dev) : device(dev) {}
+  const int device;  // CUDA ordinal whose memory this allocator hands out
   std::mutex mu;
   bool host_backend = false;
   uint64_t mem_limit = 0;
@@ -82,6 +105,7 @@ class Allocator {
     if (host_backend) return 1ull << 40;
     if (device_total) return device_total;
     if (ensure_init()) return 0;
+    DeviceGuard dg(device);
     size_t fr = 0, tot = 0;
     if (cudaMemGetInfo(&fr, &tot) != cudaSuccess) {
       (void)cudaGetLastError();
@@ -100,6 +124,7 @@ class Allocator {
       return 0;
     }
     if (int rc = ensure_init()) return rc;
+    DeviceGuard dg(device);
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, size);
     if (e != cudaSuccess) {
@@ -114,6 +139,7 @@ class Allocator {
       free((void*)base);
       return;
     }
+    DeviceGuard dg(device);
     cudaFree((void*)base);  // waits for work in flight, like vkrt's flush(true) before destroy
     (void)cudaGetLastError();
   }
@@ -164,6 +190,7 @@ class Allocator {
   // Orders `stream` after every other stream that freed into the range being reused.
   void order_after(const std::vector<cudaStream_t>& from, cudaStream_t stream) {
     if (host_backend) return;
+    DeviceGuard dg(device);  // events belong to this allocator's device, like its streams
     for (cudaStream_t s : from) {
       if (s == stream) continue;
       cudaEvent_t ev;
@@ -179,6 +206,7 @@ class Allocator {
       }
       if (cudaEventRecord(ev, s) != cudaSuccess || cudaStreamWaitEvent(stream, ev, 0) != cudaSuccess) {
         (void)cudaGetLastError();
+        DeviceGuard dg(device);
         cudaDeviceSynchronize();  // the freeing stream is gone: fall back to a full barrier
       }
       event_pool.push_back(ev);  // safe to re-record: the wait captured the recorded state
@@ -272,6 +300,7 @@ class Allocator {
 
   size_t empty_cache_locked() {
     if (!host_backend && !slabs.empty()) {
+      DeviceGuard dg(device);
       cudaDeviceSynchronize();
       (void)cudaGetLastError();
     }
@@ -287,6 +316,14 @@ class Allocator {
     return idle.size();
   }
 
+  // true when addr lies inside one of this allocator's live blocks (sets no error)
+  bool resolve_quiet(uint64_t addr) const {
+    auto it = blocks.upper_bound(addr);
+    if (it == blocks.begin()) return false;
+    --it;
+    return addr >= it->first && addr < it->first + it->second.size;
+  }
+
   // [addr, addr+n) must lie inside one live block's requested size.
   int resolve(uint64_t addr, uint64_t n) {
     auto it = blocks.upper_bound(addr);
@@ -300,9 +337,60 @@ class Allocator {
   }
 };
 
+constexpr int kMaxDevices = 64;
+std::mutex g_devices_mu;
+Allocator* g_alloc[kMaxDevices];  // never destroyed: frees may arrive during exit
+bool g_host_backend = false;      // test hook: every allocator carves host memory (device 0 only)
+uint64_t g_mem_limit = 0;         // emulated per-device limit on reserved bytes (0 = none)
+
+Allocator* A(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) {
+    fail(B2_ERR_ARG, "allocator: device ordinal " + std::to_string(dev) + " out of range");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> g(g_devices_mu);
+  if (!g_alloc[dev]) {
+    g_alloc[dev] = new Allocator(dev);
+    g_alloc[dev]->host_backend = g_host_backend;
+    g_alloc[dev]->mem_limit = g_mem_limit;
+  }
+  return g_alloc[dev];
+}
+
+int current_device() {
+  if (g_host_backend) return 0;
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    (void)cudaGetLastError();
+    d = 0;
+  }
+  return d;
+}
+
+// The allocator of the calling thread's current device (always valid: ordinals are < kMaxDevices).
 Allocator& A() {
-  static Allocator* a = new Allocator();  // never destroyed: frees may arrive during exit
-  return *a;
+  Allocator* a = A(current_device());
+  return a ? *a : *A(0);
+}
+
+// The allocator holding a live block at `addr` (the current device's first), or nullptr.
+Allocator* owner_of(uint64_t addr) {
+  Allocator& cur = A();
+  {
+    std::lock_guard<std::mutex> g(cur.mu);
+    if (cur.resolve_quiet(addr)) return &cur;
+  }
+  for (int d = 0; d < kMaxDevices; ++d) {
+    Allocator* a = nullptr;
+    {
+      std::lock_guard<std::mutex> g(g_devices_mu);
+      a = g_alloc[d];
+    }
+    if (!a || a == &cur) continue;
+    std::lock_guard<std::mutex> g(a->mu);
+    if (a->resolve_quiet(addr)) return a;
+  }
+  return nullptr;
 }
 
 }  // namespace
@@ -313,16 +401,18 @@ using namespace b2;
 extern "C" {
 
 uint64_t b2rt_max_alloc(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().max_alloc();
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.max_alloc();
 }
 
 int32_t b2rt_memory_info(uint64_t* out) {
   if (!out) return fail(B2_ERR_ARG, "memory_info: null output");
-  if (A().host_backend) {
-    std::lock_guard<std::mutex> g(A().mu);
+  Allocator& a = A();
+  if (a.host_backend) {
+    std::lock_guard<std::mutex> g(a.mu);
     out[0] = 1ull << 40;
-    out[1] = A().reserved();
+    out[1] = a.reserved();
     out[2] = 1ull << 40;
     return 0;
   }
@@ -336,40 +426,61 @@ int32_t b2rt_memory_info(uint64_t* out) {
 }
 
 uint64_t b2rt_live_bytes(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().live;
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.live;
 }
 uint64_t b2rt_peak_live_bytes(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().peak;
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.peak;
 }
 void b2rt_reset_peak_live_bytes(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  A().peak = A().live;
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  a.peak = a.live;
 }
+// The limit applies to each device's reserved bytes (every device, including ones not used yet).
 void b2rt_set_memory_limit(uint64_t bytes) {
-  std::lock_guard<std::mutex> g(A().mu);
-  A().mem_limit = bytes;
+  {
+    std::lock_guard<std::mutex> g(g_devices_mu);
+    g_mem_limit = bytes;
+  }
+  for (int d = 0; d < kMaxDevices; ++d) {
+    Allocator* a = nullptr;
+    {
+      std::lock_guard<std::mutex> g(g_devices_mu);
+      a = g_alloc[d];
+    }
+    if (!a) continue;
+    std::lock_guard<std::mutex> g(a->mu);
+    a->mem_limit = bytes;
+  }
 }
 
 uint64_t b2rt_alloc(uint64_t size) {
-  std::lock_guard<std::mutex> g(A().mu);
-  uint64_t a = 0;
-  return A().alloc(size, nullptr, &a) == 0 ? a : 0;
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  uint64_t addr = 0;
+  return a.alloc(size, nullptr, &addr) == 0 ? addr : 0;
 }
 
 int b2rt_free(uint64_t addr) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().release(addr, nullptr, false);
+  Allocator* a = owner_of(addr);
+  if (!a) return fail(B2_ERR_UNKNOWN_PTR, "free of unknown address");
+  std::lock_guard<std::mutex> g(a->mu);
+  return a->release(addr, nullptr, false);
 }
 
 int b2rt_upload(uint64_t dst, const void* src, uint64_t n) {
+  Allocator* a = owner_of(dst);
+  if (!a) return fail(B2_ERR_UNKNOWN_PTR, "unknown device address");
   {
-    std::lock_guard<std::mutex> g(A().mu);
-    if (int rc = A().resolve(dst, n)) return rc;
+    std::lock_guard<std::mutex> g(a->mu);
+    if (int rc = a->resolve(dst, n)) return rc;
   }
   stat_add(B2_STAT_UPLOAD_BYTES, n);
-  if (A().host_backend) {
+  if (a->host_backend) {
     memcpy((void*)dst, src, n);
     return 0;
   }
@@ -377,12 +488,14 @@ int b2rt_upload(uint64_t dst, const void* src, uint64_t n) {
 }
 
 int b2rt_download(void* dst, uint64_t src, uint64_t n) {
+  Allocator* a = owner_of(src);
+  if (!a) return fail(B2_ERR_UNKNOWN_PTR, "unknown device address");
   {
-    std::lock_guard<std::mutex> g(A().mu);
-    if (int rc = A().resolve(src, n)) return rc;
+    std::lock_guard<std::mutex> g(a->mu);
+    if (int rc = a->resolve(src, n)) return rc;
   }
   stat_add(B2_STAT_DOWNLOAD_BYTES, n);
-  if (A().host_backend) {
+  if (a->host_backend) {
     memcpy(dst, (const void*)src, n);
     return 0;
   }
@@ -390,12 +503,18 @@ int b2rt_download(void* dst, uint64_t src, uint64_t n) {
 }
 
 int b2rt_copy_d2d(uint64_t dst, uint64_t src, uint64_t n) {
+  Allocator* ad = owner_of(dst);
+  Allocator* as = owner_of(src);
+  if (!ad || !as) return fail(B2_ERR_UNKNOWN_PTR, "unknown device address");
   {
-    std::lock_guard<std::mutex> g(A().mu);
-    if (int rc = A().resolve(dst, n)) return rc;
-    if (int rc = A().resolve(src, n)) return rc;
+    std::lock_guard<std::mutex> g(ad->mu);
+    if (int rc = ad->resolve(dst, n)) return rc;
   }
-  if (A().host_backend) {
+  {
+    std::lock_guard<std::mutex> g(as->mu);
+    if (int rc = as->resolve(src, n)) return rc;
+  }
+  if (ad->host_backend) {
     memmove((void*)dst, (const void*)src, n);
     return 0;
   }
@@ -404,47 +523,56 @@ int b2rt_copy_d2d(uint64_t dst, uint64_t src, uint64_t n) {
 }
 
 size_t b2rt_empty_cache(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().empty_cache_locked();
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.empty_cache_locked();
 }
 
 uint64_t b2rt_reserved_bytes(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().reserved();
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.reserved();
 }
 
 size_t b2rt_live_blocks(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().blocks.size();
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.blocks.size();
 }
 
 size_t b2rt_slab_count(void) {
-  std::lock_guard<std::mutex> g(A().mu);
-  return A().slabs.size();
+  Allocator& a = A();
+  std::lock_guard<std::mutex> g(a.mu);
+  return a.slabs.size();
 }
 
 int b2rt_debug_host_backend(int on) {
-  std::lock_guard<std::mutex> g(A().mu);
-  if (!A().slabs.empty()) return fail(B2_ERR_ARG, "debug_host_backend: slabs already exist");
-  A().host_backend = on != 0;
+  std::lock_guard<std::mutex> g(g_devices_mu);
+  for (int d = 0; d < kMaxDevices; ++d)
+    if (g_alloc[d] && !g_alloc[d]->slabs.empty()) return fail(B2_ERR_ARG, "debug_host_backend: slabs already exist");
+  g_host_backend = on != 0;
+  for (int d = 0; d < kMaxDevices; ++d)
+    if (g_alloc[d]) g_alloc[d]->host_backend = g_host_backend;
   return 0;
 }
 
 void* b2_malloc(ptrdiff_t size, int device, b2_stream_t stream) {
-  (void)device;
   if (size <= 0) return nullptr;
-  std::lock_guard<std::mutex> g(A().mu);
-  uint64_t a = 0;
-  if (A().alloc((uint64_t)size, (cudaStream_t)stream, &a)) return nullptr;
-  return (void*)a;
+  Allocator* a = A(g_host_backend ? 0 : device);
+  if (!a) return nullptr;
+  std::lock_guard<std::mutex> g(a->mu);
+  uint64_t addr = 0;
+  if (a->alloc((uint64_t)size, (cudaStream_t)stream, &addr)) return nullptr;
+  return (void*)addr;
 }
 
 void b2_free(void* ptr, ptrdiff_t size, int device, b2_stream_t stream) {
   (void)size;
-  (void)device;
   if (!ptr) return;
-  std::lock_guard<std::mutex> g(A().mu);
-  A().release((uint64_t)ptr, (cudaStream_t)stream, true);
+  Allocator* a = A(g_host_backend ? 0 : device);
+  if (!a) return;
+  std::lock_guard<std::mutex> g(a->mu);
+  a->release((uint64_t)ptr, (cudaStream_t)stream, true);
 }
 
 }  // extern "C"

@@ -150,9 +150,14 @@ LaunchScope::~LaunchScope() {
   }
 }
 
+std::atomic<uint64_t> g_launch_errors{0};  // launches the runtime refused (b2rt_validation_errors)
+
 int after_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail_cuda(e, what);
+  if (e != cudaSuccess) {
+    g_launch_errors.fetch_add(1, std::memory_order_relaxed);
+    return fail_cuda(e, what);
+  }
   return 0;
 }
 
@@ -219,6 +224,36 @@ int b2rt_device_error(int reset) {
   }
   (void)cudaGetLastError();
   return v;
+}
+
+size_t b2rt_validation_errors(void) {
+  size_t n = (size_t)g_launch_errors.load(std::memory_order_relaxed);
+  if (ensure_init()) return n;
+  // read the device error word on a private non-blocking stream: waits for that copy only, not for
+  // the work in flight on other streams (a kernel still running may set it later)
+  static cudaStream_t s = [] {
+    cudaStream_t t = nullptr;
+    if (cudaStreamCreateWithFlags(&t, cudaStreamNonBlocking) != cudaSuccess) (void)cudaGetLastError();
+    return t;
+  }();
+  static int* host_word = [] {
+    int* h = nullptr;
+    if (cudaMallocHost(&h, sizeof(int)) != cudaSuccess) (void)cudaGetLastError();
+    return h;
+  }();
+  if (!s || !host_word) return n;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (cudaMemcpyFromSymbolAsync(host_word, d_error_word, sizeof(int), 0, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+      cudaStreamSynchronize(s) == cudaSuccess)
+    n += *host_word != 0 ? 1 : 0;
+  (void)cudaGetLastError();
+  return n;
+}
+
+uint32_t b2rt_coop_caps(void) {
+  if (ensure_init()) return 0;
+  return device_info().tcgen05 ? 3u : 0u;
 }
 
 uint64_t b2rt_stat(uint32_t i) { return i < B2_STAT_COUNT ? g_stats[i].load() : 0; }
