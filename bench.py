@@ -245,10 +245,19 @@ def run_ours(args, rank, world, local_rank):
     # double-buffered on the device. Outputs are read back in their storage order ([B,S,H,D] for the
     # views this library returns), so no layout kernel is added to the step.
     ke = max(10, min(K, 200))
-    e2e_ms = e2e_pipelined(pin=[x.pin_memory() for x in (qh, kh, vh, doh)], dev=dev, steps=ke, world=world)
+    local = gpu_local_cpus(dev)
+    saved = os.sched_getaffinity(0)
+    try:
+        if local:  # pinned pages are placed on the NUMA node of the thread that allocates them
+            os.sched_setaffinity(0, local)
+        e2e_ms = e2e_pipelined(pin=[x.pin_memory() for x in (qh, kh, vh, doh)], dev=dev, steps=ke, world=world)
+    finally:
+        os.sched_setaffinity(0, saved)
     e2e = {"value": world * STEP_FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "h2d_bytes_per_step": 4 * B * H * S * D * 2, "d2h_bytes_per_step": 4 * B * H * S * D * 2,
-           "ms_per_step": e2e_ms, "copies": "pinned host buffers, H2D / D2H streams overlapped with compute"}
+           "ms_per_step": e2e_ms, "copies": "pinned host buffers, H2D / D2H streams overlapped with compute",
+           "host_buffers": f"allocated from the {len(local)} GPU-local cores (NVML affinity)" if local else
+                           "allocated without NUMA placement (NVML affinity unavailable)"}
 
     # ---- per-kernel profile (separate pass): dominant kernel and its roofline -----------------------
     peaks = load_peaks()
@@ -297,6 +306,23 @@ def run_ours(args, rank, world, local_rank):
     if extra:
         result["extra"] = extra
     return result
+
+
+def gpu_local_cpus(dev):
+    """The host cores NVML reports as local to `dev` (its PCIe root's NUMA node), within this process's
+    allowed set; None when NVML cannot tell."""
+    try:
+        import pynvml
+
+        p = torch.cuda.get_device_properties(dev)
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0")
+        n = os.cpu_count() or 1
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+        cpus = {64 * i + b for i, wd in enumerate(words) for b in range(64) if (wd >> b) & 1}
+        return (cpus & os.sched_getaffinity(0)) or None
+    except Exception:
+        return None
 
 
 def e2e_pipelined(pin, dev, steps, world):
@@ -374,9 +400,9 @@ def run_dit(dev, world, blocks, tokens, steps, warmup):
     model = DiTStack(blocks=blocks, seed=0, device=dev)  # identical replicas on every rank
     trainer = LoRATrainer(model, lr=1e-4, fused_optimizer=True)
     batch = synthetic_batch(tokens=tokens, seed=1000 + rank, device=dev)  # each rank its own sample
-    # one GPU: forward + backward replayed as a CUDA graph, optimizer launched after it; several GPUs:
-    # eager, with the bucketed all-reduce hooks overlapping the backward
-    step = trainer.graphed(*batch, warmup=warmup) if world == 1 else (lambda: trainer.step(*batch))
+    # forward + backward (with the bucketed NCCL all-reduces the gradient hooks launch, when N > 1)
+    # replayed as one CUDA graph per rank, optimizer launched after each replay
+    step = trainer.graphed(*batch, warmup=warmup)
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
@@ -399,54 +425,90 @@ def run_dit(dev, world, blocks, tokens, steps, warmup):
            "loss": float(loss.item()), "lora_params": sum(p.numel() for p in trainer.params),
            "allreduce": "bucketed per block, NCCL AVG, overlapped with backward" if world > 1 else None,
            "optimizer": "multi-tensor AdamW kernel (the arithmetic of AdamW foreach=False)",
-           "timing": "CUDA graph of forward + backward, optimizer after each replay" if world == 1 else "eager"}
+           "timing": "CUDA graph of forward + backward" + (" + bucketed NCCL all-reduces" if world > 1 else "") + ", optimizer after each replay"}
     del trainer, model
     torch.cuda.empty_cache()
     return out
 
 
-def timed(fn, flush, iters=50, warm=5):
-    for _ in range(warm):
-        fn()
+def graph_timed(calls, reps=40, replays=5):
+    """Mean device ms per call when `reps` calls (cycling over `calls`, each on its own input set; the sets
+    together exceed the 126 MB L2, so every call reads its inputs from HBM) run back to back inside one CUDA
+    graph: host dispatch is out of the timed window and launches follow one another as in a training step."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in calls:
+            c()
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
-    tot = 0.0
-    for _ in range(iters):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        b.synchronize()
-        tot += a.elapsed_time(b)
-    return tot / iters
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            calls[i % len(calls)]()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) / (replays * reps)
 
 
 def run_extra(tv, dev, flush, peaks):
     """configs[0] int8-dequant linear (x[1024,2048] @ (W int8 [6144,2048] * per-row fp32 scale)^T + bias)
-    and configs[2] row kernels, each with its own roofline fraction."""
+    and configs[2] row kernels, each with its own roofline fraction. Each figure is the device time per call
+    of back-to-back calls inside one CUDA graph, cycling over input sets that together exceed L2."""
     out = {}
     g = torch.Generator().manual_seed(0)
-    x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
-    qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8).to(dev)
-    s = (torch.rand(6144, generator=g) * 9e-3 + 1e-3).to(dev)
-    bias = (torch.randn(6144, generator=g) * 0.02).to(torch.bfloat16).to(dev)
-    ms = timed(lambda: tv.int8_linear(x, qw, s, bias), flush)
+    L2 = 126e6
+
+    def nsets(bytes_per_call):
+        return max(2, int(math.ceil(2 * L2 / bytes_per_call)))
+
+    # ---- configs[0]: x 4.2 MB + W 12.6 MB + out 12.6 MB per call
+    sets = []
+    for _ in range(nsets(29.4e6)):
+        x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+        qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8).to(dev)
+        s = (torch.rand(6144, generator=g) * 9e-3 + 1e-3).to(dev)
+        bias = (torch.randn(6144, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        sets.append((x, qw, s, bias))
+    ms = graph_timed([lambda a=a: tv.int8_linear(*a) for a in sets])
     fl = 2.0 * 1024 * 6144 * 2048
     out["int8_gemm"] = {"metric": "int8-deq GEMM TFLOP/s", "config": "BASELINE configs[0] (M1024 N6144 K2048, per-row fp32 scale, bias)",
                         "value": round(fl / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 5),
-                        "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4)}
-    xs = (torch.randn(16, 1024, 1024, generator=g) * 2).to(torch.bfloat16).to(dev).requires_grad_(True)
-    gs = torch.randn(16, 1024, 1024, generator=g).to(torch.bfloat16).to(dev)
-    ys = torch.softmax(xs, -1)
-    ms_f = timed(lambda: torch.softmax(xs, -1), flush)
-    ms_b = timed(lambda: torch.ops.aten._softmax_backward_data(gs, ys, -1, torch.bfloat16), flush)
-    xl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
-    wl = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
-    bl = (0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
-    gl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
-    yl, mu, rs = torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6)
-    ms_lf = timed(lambda: torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6), flush)
-    ms_lb = timed(lambda: torch.ops.aten.native_layer_norm_backward(gl, xl, (2048,), mu, rs, wl, bl, [True, True, True]), flush)
+                        "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+                        "timing": f"CUDA graph of back-to-back calls over {len(sets)} input sets (> L2)"}
+    del sets
+
+    # ---- configs[2] softmax: x, y, g, dx bf16 [16,1024,1024] (33.5 MB each)
+    sm = []
+    for _ in range(nsets(67.1e6)):
+        xs = (torch.randn(16, 1024, 1024, generator=g) * 2).to(torch.bfloat16).to(dev)
+        gs = torch.randn(16, 1024, 1024, generator=g).to(torch.bfloat16).to(dev)
+        sm.append((xs, torch.softmax(xs, -1), gs))
+    ms_f = graph_timed([lambda a=a: torch.softmax(a[0], -1) for a in sm])
+    ms_b = graph_timed([lambda a=a: torch.ops.aten._softmax_backward_data(a[2], a[1], -1, torch.bfloat16) for a in sm])
+    del sm
+
+    # ---- configs[2] LayerNorm: x, g bf16 [1024, 2048], w ~N(1,0.1), b ~N(0,0.1), eps 1e-6
+    ln = []
+    for _ in range(nsets(8.4e6)):
+        xl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+        wl = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
+        bl = (0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
+        gl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
+        _, mu, rs = torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6)
+        ln.append((xl, wl, bl, gl, mu, rs))
+    ms_lf = graph_timed([lambda a=a: torch.native_layer_norm(a[0], (2048,), a[1], a[2], 1e-6) for a in ln])
+    ms_lb = graph_timed([lambda a=a: torch.ops.aten.native_layer_norm_backward(a[3], a[0], (2048,), a[4], a[5], a[1], a[2],
+                                                                               [True, True, True]) for a in ln])
+    nln = len(ln)
+    del ln
     hbm = peaks["hbm_gbs"]
 
     def gbs(nbytes, ms_):
@@ -454,9 +516,13 @@ def run_extra(tv, dev, flush, peaks):
 
     out["rows"] = {"metric": "row kernels GB/s (algorithmic bytes)", "config": "BASELINE configs[2]", "peak_gbs": hbm,
                    "softmax_fwd": gbs(67.1e6, ms_f), "softmax_bwd": gbs(100.7e6, ms_b),
-                   "layernorm_fwd": gbs(8.40e6, ms_lf), "layernorm_bwd": gbs(12.6e6, ms_lb)}
+                   "layernorm_fwd": gbs(8.40e6, ms_lf), "layernorm_bwd": gbs(12.6e6, ms_lb),
+                   "us_per_call": {"softmax_fwd": round(ms_f * 1e3, 2), "softmax_bwd": round(ms_b * 1e3, 2),
+                                   "layernorm_fwd": round(ms_lf * 1e3, 2), "layernorm_bwd": round(ms_lb * 1e3, 2)},
+                   "timing": f"CUDA graph of back-to-back calls over input sets > L2 (LayerNorm {nln} sets)"}
     for k2 in ("softmax_fwd", "softmax_bwd", "layernorm_fwd", "layernorm_bwd"):
         out["rows"][k2 + "_frac"] = round(out["rows"][k2] / hbm, 4)
+    torch.cuda.empty_cache()
     return out
 
 
@@ -487,6 +553,70 @@ def cpu_baseline(budget_s=12.0):
     return {"value": round(fl / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"{reps} full configs[1] fwd+bwd passes (torch CPU SDPA, bf16) in {dt:.1f} s",
             "cpu": _cpu_model()}
+
+
+def _cpu_time(fn, budget_s):
+    """Mean seconds of fn() over about budget_s seconds (one untimed warm-up call); returns (s, reps)."""
+    fn()
+    t0 = time.perf_counter()
+    fn()
+    dt1 = time.perf_counter() - t0
+    reps = int(max(1, min(200, budget_s / max(dt1, 1e-4))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps, reps
+
+
+def cpu_baselines_extra(budget_s=6.0):
+    """The reference's CPU path (stock PyTorch CPU ATen in bf16 on all host threads) for the other BASELINE
+    configs, each a bounded sample: configs[0] per-row dequant + addmm; configs[2] softmax / LayerNorm
+    forward and backward; configs[3] the DiT block LoRA step; configs[4] one block at 4096 tokens, scaled
+    by 28 (an extrapolation, stated as such)."""
+    import oracle.dit_cpu as dc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cpu = _cpu_model()
+    out = {}
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16)
+    qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8)
+    s = torch.rand(6144, generator=g) * 9e-3 + 1e-3
+    bias = (torch.randn(6144, generator=g) * 0.02).to(torch.bfloat16)
+    sec, reps = _cpu_time(lambda: torch.addmm(bias, x, (qw.float() * s[:, None]).to(torch.bfloat16).t()), budget_s)
+    out["int8_gemm"] = {"value": round(2.0 * 1024 * 6144 * 2048 / sec / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+                        "kind": "port", "sample": f"{reps} full configs[0] calls (per-row dequant + torch.addmm, bf16)",
+                        "cpu": cpu}
+    xs = (torch.randn(16, 1024, 1024, generator=g) * 2).to(torch.bfloat16)
+    gs = torch.randn(16, 1024, 1024, generator=g).to(torch.bfloat16)
+    ys = torch.softmax(xs, -1)
+    xl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16)
+    wl = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    bl = (0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16)
+    gl = torch.randn(1024, 2048, generator=g).to(torch.bfloat16)
+    _, mu, rs = torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6)
+    rows = {}
+    for name, nbytes, fn in (("softmax_fwd", 67.1e6, lambda: torch.softmax(xs, -1)),
+                             ("softmax_bwd", 100.7e6, lambda: torch.ops.aten._softmax_backward_data(gs, ys, -1, torch.bfloat16)),
+                             ("layernorm_fwd", 8.40e6, lambda: torch.native_layer_norm(xl, (2048,), wl, bl, 1e-6)),
+                             ("layernorm_bwd", 12.6e6, lambda: torch.ops.aten.native_layer_norm_backward(
+                                 gl, xl, (2048,), mu, rs, wl, bl, [True, True, True]))):
+        sec, _ = _cpu_time(fn, budget_s / 4)
+        rows[name] = round(nbytes / sec / 1e9, 2)
+    out["rows"] = dict(rows, unit="GB/s", cores=threads, kind="port", cpu=cpu,
+                       sample="configs[2] shapes, each op timed for about %.1f s" % (budget_s / 4))
+    dit = {}
+    for label, tokens, blocks in (("config3_block", 1024, 1), ("config4_stack", 4096, 28)):
+        p = dc.make_block(seed=0)
+        step = dc.make_step(p)
+        batch = dc.synthetic_batch(tokens=tokens, seed=1)
+        sec, reps = _cpu_time(lambda: step(*batch), budget_s)
+        dit[label] = {"ms_per_step": round(sec * 1e3 * blocks, 1), "unit": "ms", "cores": threads, "kind": "port",
+                      "cpu": cpu, "sample": f"{reps} one-block LoRA steps at {tokens} tokens (CPU PyTorch, bf16)" +
+                      (f", scaled by {blocks} blocks (an extrapolation)" if blocks > 1 else "")}
+    out["dit_lora_step"] = dit
+    return out
 
 
 def _cpu_model():
@@ -599,6 +729,15 @@ def _main(json_out):
     res = run_ours(args, rank, world, local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline()
+        ex = res.get("extra")
+        if ex:  # the other configs' CPU baselines beside their GPU lines
+            cb = cpu_baselines_extra()
+            for key in ("int8_gemm", "rows"):
+                if key in ex:
+                    ex[key]["cpu_baseline"] = cb[key]
+            for label, v in cb["dit_lora_step"].items():
+                if label in ex.get("dit_lora_step", {}):
+                    ex["dit_lora_step"][label]["cpu_baseline"] = v
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -227,6 +227,16 @@ typedef struct b2_int8_gemm_args {
    * second kernel); NULL or too small: no split */
   void* workspace;
   int64_t workspace_bytes;
+  /* Fused activation epilogue of the DiT MLP (new; the reference runs GELU as its own elementwise
+   * kernels, csrc/ops_ew.cpp:321-326 and :352). aux is bf16 [M, out_cols] with row stride aux_ld.
+   *   0: none.
+   *   1 (forward form): out = h = x @ W~^T + bias and aux = gelu_tanh(h) of the bf16-rounded h.
+   *   2 (transposed form): out = bf16(dY @ W~) * gelu_tanh'(aux), aux = the forward's h.
+   * GELU is the tanh approximation (F.gelu(approximate="tanh")). No split-K with an epilogue. */
+  int32_t epilogue;
+  int32_t pad_;
+  void* aux;
+  int64_t aux_ld;
 } b2_int8_gemm_args;
 int b2_int8_gemm(const b2_int8_gemm_args* args, b2_stream_t stream);
 uint64_t b2_int8_gemm_workspace_bytes(const b2_int8_gemm_args* args);

@@ -32,7 +32,8 @@ class Int8Args(ctypes.Structure):
     _fields_ = [("x", ctypes.c_void_p), ("q", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("bias", ctypes.c_void_p),
                 ("out", ctypes.c_void_p), ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
                 ("x_ld", ctypes.c_int64), ("out_ld", ctypes.c_int64), ("scale_layout", ctypes.c_int32),
-                ("transpose_w", ctypes.c_int32), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64)]
+                ("transpose_w", ctypes.c_int32), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
+                ("epilogue", ctypes.c_int32), ("pad_", ctypes.c_int32), ("aux", ctypes.c_void_p), ("aux_ld", ctypes.c_int64)]
 
 
 @pytest.fixture(scope="module")

@@ -66,6 +66,65 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _worker_graphed(rank, world, port, q):
+    """Two identical trainers per rank: one steps eagerly, one replays its forward + backward (with the
+    captured bucket all-reduces) as a CUDA graph; after three steps both hold the same LoRA parameters."""
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        from torch_vulkan_b200.dit import DiTStack, LoRATrainer
+
+        batch = _batch(rank, dev)
+        eager = LoRATrainer(DiTStack(blocks=2, seed=0, device=dev, **KW), lr=1e-3, fused_optimizer=True)
+        le = [float(eager.step(*batch).item()) for _ in range(3)]
+        pe = torch.cat([p.detach().float().flatten() for p in eager.params]).cpu()
+        gtr = LoRATrainer(DiTStack(blocks=2, seed=0, device=dev, **KW), lr=1e-3, fused_optimizer=True)
+        step = gtr.graphed(*batch, warmup=1)  # one eager warm-up step, then captured steps
+        lg = [float(step().item()) for _ in range(2)]
+        pg = torch.cat([p.detach().float().flatten() for p in gtr.params]).cpu()
+        torch.cuda.synchronize()
+        del step, gtr._graph  # graphs holding NCCL work go before the process group
+        q.put((rank, le, lg, pe.numpy(), pg.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, world=2):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return {o[0]: o[1:] for o in out}
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nccl_graphed_step_matches_eager_step():
+    res = _spawn(_worker_graphed)
+    for r in range(2):
+        le, lg, pe, pg = res[r]
+        # graphed steps 2 and 3 against eager steps 2 and 3 (warm-up = eager step 1)
+        assert max(abs(a - b) / abs(b) for a, b in zip(lg, le[1:])) < 1e-3, (le, lg)
+        pe, pg = torch.from_numpy(pe).double(), torch.from_numpy(pg).double()
+        assert ((pg - pe).norm() / pe.norm()).item() < 1e-3
+    # replicas identical across ranks, eager and graphed
+    assert torch.equal(torch.from_numpy(res[0][2]), torch.from_numpy(res[1][2]))
+    assert torch.equal(torch.from_numpy(res[0][3]), torch.from_numpy(res[1][3]))
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_nccl_bucketed_average_matches_single_process():
     import torch.multiprocessing as mp

@@ -79,8 +79,8 @@ def test_slab_allocator_serves_a_dit_step():
     assert slab["slabs"] >= 1
     assert slab["reused"] and slab["waits"] >= 1 and slab["b_ok"]
     assert slab["live_after_free"] == 0
-    assert slab["peak"] > 1 << 30  # the block's int8 weights, activations and gradients
-    assert slab["slabs_after_step"] >= 2 and slab["reserved"] >= slab["peak"]
+    assert slab["peak"] > 256 << 20  # the block's int8 weights (63 M), activations and gradients
+    assert slab["slabs_after_step"] >= 1 and slab["reserved"] >= slab["peak"]
     assert slab["validation_errors"] == 0
     ref = run_child(False)
     for a, b in zip(slab["losses"], ref["losses"]):

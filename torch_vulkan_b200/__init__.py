@@ -294,6 +294,34 @@ def int8_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: tor
     return _Int8Linear.apply(x, q, scale, bias)
 
 
+class _Int8GeluMLP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, q1, s1, b1, q2, s2, b2):
+        act, h = torch.ops.b2.int8_linear_gelu_fwd(x, q1, s1, b1)  # one GEMM: h and gelu(h)
+        y = torch.ops.b2.int8_linear_fwd(act, q2, s2, b2)
+        ctx.save_for_backward(q1, s1, q2, s2, h)
+        ctx.bias_grad = (b1 is not None and ctx.needs_input_grad[3], b2 is not None and ctx.needs_input_grad[6])
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        q1, s1, q2, s2, h = ctx.saved_tensors
+        gy = gy.contiguous()
+        dh = torch.ops.b2.int8_linear_dx_gelu(gy, q2, s2, h)  # one GEMM: (gy @ W2) * gelu'(h)
+        gx = torch.ops.b2.int8_linear_dx(dh, q1, s1) if ctx.needs_input_grad[0] else None
+        gb1 = dh.reshape(-1, dh.shape[-1]).sum(0) if ctx.bias_grad[0] else None
+        gb2 = gy.reshape(-1, gy.shape[-1]).sum(0) if ctx.bias_grad[1] else None
+        return gx, None, None, gb1, None, None, gb2
+
+
+def int8_mlp(x, q1, s1, b1, q2, s2, b2):
+    """fc2(gelu_tanh(fc1(x))) over frozen int8 weights (the DiT block's MLP), with the GELU fused into
+    the GEMM epilogues: fc1's epilogue writes the pre-activation h and gelu(h), and in the backward fc2's
+    dX epilogue multiplies by gelu'(h). No separate GELU kernels and no extra pass over the
+    [tokens, mlp] activation. Differentiable in x (and the biases)."""
+    return _Int8GeluMLP.apply(x, q1, s1, b1, q2, s2, b2)
+
+
 if os.environ.get("B2_DISABLE", "0") in ("", "0"):
     enable(True)
 

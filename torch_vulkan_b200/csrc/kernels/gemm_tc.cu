@@ -96,20 +96,50 @@ struct TcParams {
   // c_tma: C is written through the tensor map tmC (32-column x 32-row boxes, 64 B swizzle) from a
   // per-warp shared-memory staging tile; c3d: that map has a batch dimension
   int c_tma, c3d;
+  // fused activation epilogue (bf16 output written through tmC, no split-K):
+  //   EPI_GELU:     C = h = acc + bias, and aux = gelu_tanh(h) (both bf16; gelu of the rounded h)
+  //   EPI_GELU_BWD: C = bf16(acc) * gelu_tanh'(aux) (aux = the forward's h)
+  int epi;
+  void* aux;
+  int64_t aux_ld;
 };
 
-template <int BN, int DEQ, int MSUB>
+enum : int { EPI_NONE = 0, EPI_GELU = 1, EPI_GELU_BWD = 2 };
+
+// GELU with the tanh approximation (Hendrycks & Gimpel 2016): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+// tanh from the hardware approximation (relative error ~2^-11, below a bf16 ulp).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kGeluK0 = 0.7978845608028654f, kGeluK1 = 0.044715f;
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float t = tanh_fast(kGeluK0 * (x + kGeluK1 * x * x * x));
+  return 0.5f * x * (1.f + t);
+}
+__device__ __forceinline__ float gelu_tanh_grad(float x) {
+  const float t = tanh_fast(kGeluK0 * (x + kGeluK1 * x * x * x));
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * kGeluK0 * (1.f + 3.f * kGeluK1 * x * x);
+}
+__device__ __forceinline__ float bf16_round(float v) { return bf16_bits_to_f32(f32_to_bf16_bits(v)); }
+
+// CG = CTAs per MMA: 1, or 2 for a cluster pair (cta_group::2) whose MMAs are M = 256 with each CTA
+// staging its own 128-row A halves and half (BN / 2 rows) of the B tile; the pair covers 2 * BMT x BN.
+template <int BN, int DEQ, int MSUB, int CG = 1>
 struct Cfg {
-  static constexpr int BMT = BM * MSUB;             // rows of the CTA tile
+  static constexpr int BMT = BM * MSUB;             // rows of the CTA tile (this CTA's share of a pair)
+  static constexpr int BNC = BN / CG;               // B rows (output columns) this CTA stages
   static constexpr int A_BYTES = BMT * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int R_BYTES = DEQ ? BN * BK : 0;  // raw int8 tile
+  static constexpr int B_BYTES = BNC * BK * 2;
+  static constexpr int R_BYTES = DEQ ? BNC * BK : 0;  // raw int8 tile
   // bf16: a TMA stage holds A and B. int8: three rings. A stages (released by the MMAs), raw int8
   // tiles (released by the dequant warps as soon as they have converted one, so those loads run
   // ahead of the MMAs) and NB dequantised bf16 B tiles (released by the MMAs).
   static constexpr int STAGE = A_BYTES + (DEQ ? 0 : B_BYTES);
   static constexpr int NB = DEQ;  // int8: depth of the dequantised B ring (DEQ = 0: the bf16 path)
   static constexpr int NR = DEQ ? (R_BYTES >= 11264 ? 3 : 4) : 0;  // int8: depth of the raw ring
+  static_assert(CG == 1 || (DEQ && BNC % 8 == 0), "CTA pairs: int8 kernels, B halves of whole 8-row groups");
   // epilogue: per warp one staging buffer (32 rows x 32 16-bit columns) and the tile's bias row
   static constexpr int EPI_BYTES = 4 * 2048 + 4 * 512;
   static constexpr int BUDGET = 224 * 1024 - NB * B_BYTES - NR * R_BYTES - EPI_BYTES;
@@ -166,11 +196,12 @@ __device__ __forceinline__ void dequant16(const int4& raw, float s, uint32_t* w)
   }
 }
 
-template <int BN, bool BF16, int DEQ, int MSUB>
-__global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
+template <int BN, bool BF16, int DEQ, int MSUB, int CG>
+__global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, TcParams p) {
-  using C = Cfg<BN, DEQ, MSUB>;
+  using C = Cfg<BN, DEQ, MSUB, CG>;
+  constexpr int BNC = C::BNC;
   constexpr int S = C::STAGES;
   constexpr int NDQ = C::DEQ_WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
@@ -193,6 +224,15 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_tiles = p.m_tiles * p.n_tiles * (int)p.batch;
   const int total_work = total_tiles * p.ksplit;
+  // CTA pairs: rank 0 (the leader) issues the MMAs and owns the barriers that gather both CTAs' work;
+  // both CTAs of a pair walk the same work items (pair index = blockIdx.x / CG)
+  const uint32_t rank = CG == 2 ? tc::cluster_ctarank() : 0u;
+  const int unit0 = (int)blockIdx.x / CG, nunits = (int)gridDim.x / CG;
+  // leader-side barrier addresses as seen from this CTA (its own shared::cta addresses when CG == 1)
+  auto leader_bar = [&](uint64_t* bar) -> uint32_t {
+    return CG == 2 ? tc::mapa_shared(tc::smem_u32(bar), 0u) : tc::smem_u32(bar);
+  };
+  auto wait_bar = [&](uint64_t* bar, uint32_t parity) -> bool { return tc::mbar_wait(bar, parity, p.err); };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -200,7 +240,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       tc::mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < NB; ++i) {
-      tc::mbar_init(&bready[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS : 1);  // one arrival per dequant warp
+      // one arrival per dequant warp (of both CTAs of a pair)
+      tc::mbar_init(&bready[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS * CG : 1);
       tc::mbar_init(&bfree[i], 1);
     }
     for (int i = 0; i < NR; ++i) {
@@ -209,14 +250,20 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&tfull[i], 1);
-      tc::mbar_init(&tempty[i], 128);
+      tc::mbar_init(&tempty[i], CG == 2 ? 4 * CG : 128);  // pairs: one arrival per epilogue warp
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
+  if (CG == 2) tc::cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tc::tmem_relinquish();
+    if (CG == 2) {
+      tc::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -233,7 +280,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     b = t / per_b;
     int r = t - b * per_b;
     int mt = r % p.m_tiles, nt = r / p.m_tiles;
-    m0 = mt * C::BMT;
+    m0 = mt * C::BMT * CG;  // first row of the (pair) tile; this CTA's rows start at m0 + rank * BMT
     n0 = nt * BN;
   };
 
@@ -247,21 +294,34 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       uint32_t phase = 0;
       int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       bool ok = true;
-      for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x) {
+      const uint32_t full0 = leader_bar(&full[0]);  // the leader's full[s] is full0 + 8 * s
+      for (int t = unit0; t < total_work && ok; t += nunits) {
         int m0, n0, b, kb0, kb1;
         tile_coords(t, m0, n0, b);
         k_range(t, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!tc::mbar_wait(&empty[stage], phase ^ 1, p.err) || *abort_flag) {
+          if (!wait_bar(&empty[stage], phase ^ 1) || *abort_flag) {
             ok = false;
             *abort_flag = 1;
             break;
           }
           uint8_t* sa = smem + stage * C::STAGE;
           uint8_t* sb = sa + C::A_BYTES;
+          const int k0 = kb * BK;
+          if (CG == 2) {
+            // this CTA's BMT rows of A land in its own shared memory and count on the leader's full
+            // barrier, which the leader arms for both CTAs' bytes
+            if (rank == 0) tc::mbar_arrive_expect_tx(&full[stage], (uint32_t)(C::STAGE * CG));
+            tc::tma_load_2d_pair(sa, &tmA, full0 + 8u * (uint32_t)stage, k0, m0 + (int)rank * C::BMT);
+            issued[stage] += 1;
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           const uint32_t bytes = C::STAGE;
           tc::mbar_arrive_expect_tx(&full[stage], bytes);
-          const int k0 = kb * BK;
           if (!p.a_mn) {  // one box of BMT rows x 64 k
             if (p.a3d) tc::tma_load_3d(sa, &tmA, &full[stage], k0, m0, b);
             else tc::tma_load_2d(sa, &tmA, &full[stage], k0, m0);
@@ -291,17 +351,25 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
         }
       }
-      if (!ok) {
+      if (!ok && rank == 0) {
         // Drain: every issued load completes on its stage's full barrier. Stage s saw issued[s]
         // arms, so its phase count is issued[s]; wait (bounded) for the last one.
         for (int s = 0; s < S; ++s)
           if (issued[s] > 0) tc::mbar_wait(&full[s], (uint32_t)((issued[s] - 1) & 1), nullptr);
       }
+      if (ok && CG == 2) {
+        // pairs: the leader's last MMA commits arrive on this CTA's empty barriers; wait for them
+        // before the CTA can leave, so no arrival reaches a CTA that has exited
+        for (int s = 0; s < S; ++s)
+          if (issued[s] > 0) wait_bar(&empty[s], (uint32_t)((issued[s] - 1) & 1));
+      }
     }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer ---------------------------------------------
-    if (lane == 0) {
-      constexpr uint32_t IDESC_BASE = tc::idesc_f16(BM, BN, BF16, false, false);
+    // (pairs: only the leader issues; the peer's warp 1 only allocates and frees its TMEM)
+    if (lane == 0 && rank == 0) {
+      // pairs: M = 256 per MMA (128 rows from each CTA), N = BN (BN / 2 B rows from each CTA)
+      constexpr uint32_t IDESC_BASE = tc::idesc_f16(BM * CG, BN, BF16, false, false);
       const uint32_t idesc = IDESC_BASE | ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16);
       // K-major: +32 B per 16-element K step inside the 128 B swizzle row (LBO unused);
       // MN-major: +16 rows of 128 B per step, LBO = distance between 64-element MN chunks.
@@ -312,11 +380,11 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       int it = 0;
       int gk = 0;  // K blocks consumed so far (B ring position)
       bool ok = true;
-      for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x, ++it) {
+      for (int t = unit0; t < total_work && ok; t += nunits, ++it) {
         int kb0, kb1;
         k_range(t, kb0, kb1);
         const int acc = it % NACC;
-        if (!tc::mbar_wait(&tempty[acc], ((it / NACC) & 1) ^ 1, p.err) || *abort_flag) {
+        if (!wait_bar(&tempty[acc], ((it / NACC) & 1) ^ 1) || *abort_flag) {
           ok = false;
           break;
         }
@@ -324,8 +392,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         const uint32_t d = tbase + (uint32_t)(acc * C::ACC_COLS);
         for (int kb = kb0; kb < kb1; ++kb) {
           const int bb = gk % NB;
-          if (!tc::mbar_wait(&full[stage], phase, p.err) ||
-              (DEQ && !tc::mbar_wait(&bready[bb], (uint32_t)((gk / NB) & 1), p.err))) {
+          if (!wait_bar(&full[stage], phase) || (DEQ && !wait_bar(&bready[bb], (uint32_t)((gk / NB) & 1)))) {
             ok = false;
             break;
           }
@@ -339,12 +406,22 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t bd = tc::sdesc_at(bd0, k * b_step);
 #pragma unroll
-            for (int ms = 0; ms < MSUB; ++ms)  // M sub-tile ms at +ms*16 KB (K-major rows / MN-major chunks)
-              tc::mma_f16_ss(d + ms * C::SUB_COLS, tc::sdesc_at(ad0, ms * 16384 + k * a_step), bd, idesc,
-                             k > 0 ? 1u : acc0);
+            for (int ms = 0; ms < MSUB; ++ms) {  // M sub-tile ms at +ms*16 KB (K-major rows / MN-major chunks)
+              if (CG == 2)
+                tc::mma_f16_ss_pair(d + ms * C::SUB_COLS, tc::sdesc_at(ad0, ms * 16384 + k * a_step), bd, idesc,
+                                    k > 0 ? 1u : acc0);
+              else
+                tc::mma_f16_ss(d + ms * C::SUB_COLS, tc::sdesc_at(ad0, ms * 16384 + k * a_step), bd, idesc,
+                               k > 0 ? 1u : acc0);
+            }
           }
-          tc::mma_commit(&empty[stage]);
-          if (DEQ) tc::mma_commit(&bfree[bb]);
+          if (CG == 2) {  // release the stage and the B buffer in both CTAs
+            tc::mma_commit_pair(&empty[stage], (uint16_t)3);
+            tc::mma_commit_pair(&bfree[bb], (uint16_t)3);
+          } else {
+            tc::mma_commit(&empty[stage]);
+            if (DEQ) tc::mma_commit(&bfree[bb]);
+          }
           ++gk;
           if (++stage == S) {
             stage = 0;
@@ -352,7 +429,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
         }
         if (!ok) break;
-        tc::mma_commit(&tfull[acc]);
+        if (CG == 2) tc::mma_commit_pair(&tfull[acc], (uint16_t)3);
+        else tc::mma_commit(&tfull[acc]);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -367,10 +445,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     OutT* bsm = reinterpret_cast<OutT*>(smem + C::OFF_EPI + 4 * 2048 + (warp - 2) * 512);
     const bool bias_row = p.has_bias && p.bias_sm == 0 && (p.batch == 1 || p.bias_sb == 0) && p.bias_sn == 1 &&
                           (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
-    for (int t = blockIdx.x; t < total_work; t += gridDim.x, ++it) {
+    const uint32_t tempty0 = leader_bar(&tempty[0]);  // pairs: the leader's tempty[a] is tempty0 + 8 * a
+    for (int t = unit0; t < total_work; t += nunits, ++it) {
       const int acc = it % NACC;
       int m0, n0, b;
       tile_coords(t, m0, n0, b);
+      m0 += (int)rank * C::BMT;  // pairs: this CTA's TMEM holds its own BMT rows of the pair tile
       if (bias_row) {
         const OutT* bsrc = (const OutT*)p.bias + n0;
         for (int c = lane; c < BN / 8; c += 32) {
@@ -386,7 +466,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         }
         __syncwarp();
       }
-      if (!tc::mbar_wait(&tfull[acc], (it / NACC) & 1, p.err) || *abort_flag) {
+      if (!wait_bar(&tfull[acc], (it / NACC) & 1) || *abort_flag) {
         *abort_flag = 1;
         break;
       }
@@ -460,6 +540,43 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
                   for (int j = 0; j < 32; ++j)
                     if (col0 + j < p.N)
                       r[j] = __float_as_uint(__uint_as_float(r[j]) + p.beta * to_f32(brow[(col0 + j) * p.bias_sn]));
+                }
+              }
+              if (p.epi != EPI_NONE && row_ok) {
+                // fused GELU: each lane's 32 columns of its row are 64 contiguous bytes of aux
+                OutT* arow = (OutT*)p.aux + row * p.aux_ld + col0;
+                const bool full = col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(arow) & 15) == 0;
+                if (p.epi == EPI_GELU) {  // aux = gelu(h) of the bf16-rounded h the main output holds
+                  uint32_t a[16];
+#pragma unroll
+                  for (int j = 0; j < 16; ++j)
+                    a[j] = pack_out(gelu_tanh(bf16_round(__uint_as_float(r[2 * j]))),
+                                    gelu_tanh(bf16_round(__uint_as_float(r[2 * j + 1]))), BF16);
+                  if (full) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                      reinterpret_cast<uint4*>(arow)[j] = make_uint4(a[4 * j], a[4 * j + 1], a[4 * j + 2], a[4 * j + 3]);
+                  } else {
+                    const OutT* ah = reinterpret_cast<const OutT*>(a);
+                    for (int j = 0; j < 32 && col0 + j < p.N; ++j) arow[j] = ah[j];
+                  }
+                } else {  // EPI_GELU_BWD: dh = bf16(da) * gelu'(h), h read from aux
+                  float hv[32];
+                  if (full) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                      const uint4 raw = reinterpret_cast<const uint4*>(arow)[j];
+                      const OutT* hh = reinterpret_cast<const OutT*>(&raw);
+#pragma unroll
+                      for (int e = 0; e < 8; ++e) hv[8 * j + e] = to_f32(hh[e]);
+                    }
+                  } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) hv[j] = col0 + j < p.N ? to_f32(arow[j]) : 0.f;
+                  }
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    r[j] = __float_as_uint(bf16_round(__uint_as_float(r[j])) * gelu_tanh_grad(hv[j]));
                 }
               }
               uint8_t* buf = stg;
@@ -543,7 +660,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         if constexpr (BN % 32 != 0) chunk(std::integral_constant<int, 16>{}, (BN / 32) * 32);
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(&tempty[acc]);
+      if (CG == 2) {  // one arrival per warp on the leader's barrier, after every lane's TMEM reads
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cluster(tempty0 + 8u * (uint32_t)acc);
+      } else {
+        tc::mbar_arrive(&tempty[acc]);
+      }
     }
     if (lane == 0) tc::bulk_wait0();  // every C store of this warp complete before the CTA exits
   } else if (DEQ && warp == C::R_WARP) {
@@ -553,10 +675,11 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
       uint32_t rph = 0;
       int issued[4] = {0, 0, 0, 0};
       bool ok = true;
-      for (int t = blockIdx.x; t < total_work && ok; t += gridDim.x) {
+      for (int t = unit0; t < total_work && ok; t += nunits) {
         int m0, n0, b, kb0, kb1;
         tile_coords(t, m0, n0, b);
         k_range(t, kb0, kb1);
+        n0 += (int)rank * BNC;  // pairs: this CTA stages B rows [n0 + rank * BN/2, + BN/2)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&rempty[rs], rph ^ 1, p.err) || *abort_flag) {
             ok = false;
@@ -565,7 +688,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           }
           uint8_t* sr = smem + C::OFF_R + rs * C::R_BYTES;
           tc::mbar_arrive_expect_tx(&rfull[rs], (uint32_t)C::R_BYTES);
-          // raw int8 W tile: forward box {64 (k), BN (n)}; transposed box {BN (k_feat), 64 (n_feat)}
+          // raw int8 W tile: forward box {64 (k), BNC (n)}; transposed box {BNC (k_feat), 64 (n_feat)}
           if (!p.b_mn) tc::tma_load_2d(sr, &tmB, &rfull[rs], kb * BK, n0);
           else tc::tma_load_2d(sr, &tmB, &rfull[rs], n0, kb * BK);
           issued[rs] += 1;
@@ -584,15 +707,17 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
     const int dw = warp - 6 - (warp > 9 ? 1 : 0) - (warp > 13 ? 1 : 0);  // 0 .. 7
     const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
     int gk = 0;  // K blocks dequantised so far (B ring position)
-    constexpr int FIPT = (BN * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
+    constexpr int FIPT = (BNC * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
     float fsc[FIPT];
-    constexpr int IPT = (64 * (BN / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // transposed items per thread
+    constexpr int IPT = (64 * (BNC / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // transposed items per thread
     float sc[IPT];
-    for (int t = blockIdx.x; t < total_work; t += gridDim.x) {
+    const uint32_t bready0 = leader_bar(&bready[0]);  // pairs: the leader's bready[i] is bready0 + 8 * i
+    bool ok = true;
+    for (int t = unit0; t < total_work && ok; t += nunits) {
       int m0, n0, b, kb0, kb1;
       tile_coords(t, m0, n0, b);
       k_range(t, kb0, kb1);
-      bool ok = true;
+      n0 += (int)rank * BNC;  // pairs: this CTA dequantises B rows [n0 + rank * BN/2, + BN/2)
       for (int kb = kb0; kb < kb1; ++kb) {
         // forward scales, loaded before the waits so that their latency overlaps them: block-64
         // scales change with the K block, per-row scales are loaded once per tile
@@ -602,7 +727,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
             const int i = dt + u * NDQ;
             const int64_t gn = (int64_t)n0 + (i >> 2);
             fsc[u] = 0.f;
-            if (i < BN * 4 && gn < p.deq_rows)
+            if (i < BNC * 4 && gn < p.deq_rows)
               fsc[u] = p.scale_layout == 0
                            ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[gn * p.scale_nb + kb])
                            : reinterpret_cast<const float*>(p.scale)[gn];
@@ -614,11 +739,11 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
 #pragma unroll
           for (int u = 0; u < IPT; ++u) {  // every scale load in flight before the first is used
             const int e = dt + u * NDQ;
-            const int i = e / (BN / 16), qd = e % (BN / 16);
+            const int i = e / (BNC / 16), qd = e % (BNC / 16);
             const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
             const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
             sc[u] = 0.f;
-            if (e < 64 * (BN / 16) && nf < p.deq_rows)
+            if (e < 64 * (BNC / 16) && nf < p.deq_rows)
               sc[u] = p.scale_layout == 0
                           ? bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.scale)[nf * p.scale_nb + (kf >> 6)])
                           : reinterpret_cast<const float*>(p.scale)[nf];
@@ -629,19 +754,19 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
           break;
         }
         const int bb = gk % NB;
-        if (!tc::mbar_wait(&bfree[bb], (uint32_t)(((gk / NB) & 1) ^ 1), p.err)) {
+        if (!wait_bar(&bfree[bb], (uint32_t)(((gk / NB) & 1) ^ 1))) {
           ok = false;
           break;
         }
         uint8_t* sb = smem + C::OFF_B + bb * C::B_BYTES;
         const uint8_t* sr = smem + C::OFF_R + rs * C::R_BYTES;
         if (!p.b_mn) {
-          // forward: raw [BN rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
+          // forward: raw [BNC rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
 #pragma unroll
           for (int u = 0; u < FIPT; ++u) {
             const int i = dt + u * NDQ;
-            if (i >= BN * 4) break;
+            if (i >= BNC * 4) break;
             const int n = i >> 2, j = i & 3;  // 16 int8 = k 16j..16j+15
             const float s = fsc[u];
             const int4 raw = *reinterpret_cast<const int4*>(sr + n * 64 + j * 16);
@@ -653,15 +778,15 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
             *reinterpret_cast<uint4*>(rowp + ((c1 ^ (n & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
           }
         } else {
-          // backward: raw [64 rows i (n_feat)][BN bytes (k_feat = n_gemm)]; B stage MN-major SW128:
+          // backward: raw [64 rows i (n_feat)][BNC bytes (k_feat = n_gemm)]; B stage MN-major SW128:
           // chunk j = n_gemm/64 at j*8192, row i at i*128, 16 B granule g at ((g ^ (i & 7)) * 16).
 #pragma unroll
           for (int u = 0; u < IPT; ++u) {
             const int e = dt + u * NDQ;
-            if (e >= 64 * (BN / 16)) break;
-            const int i = e / (BN / 16), qd = e % (BN / 16);
+            if (e >= 64 * (BNC / 16)) break;
+            const int i = e / (BNC / 16), qd = e % (BNC / 16);
             const float s = sc[u];
-            const int4 raw = *reinterpret_cast<const int4*>(sr + i * BN + qd * 16);
+            const int4 raw = *reinterpret_cast<const int4*>(sr + i * BNC + qd * 16);
             uint32_t w[8];
             dequant16(raw, s, w);
             const int chunk = (qd * 16) >> 6, g0 = ((qd * 16) & 63) >> 3;
@@ -676,11 +801,19 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           tc::mbar_arrive(&rempty[rs]);
-          tc::mbar_arrive(&bready[bb]);
+          if (CG == 2) tc::mbar_arrive_cluster(bready0 + 8u * (uint32_t)bb);
+          else tc::mbar_arrive(&bready[bb]);
         }
         ++gk;
       }
-      if (!ok) break;
+    }
+    if (ok && CG == 2 && dw == 0 && lane == 0) {
+      // pairs: the leader's last commits arrive on this CTA's bfree barriers; wait for them before
+      // the CTA can leave
+      for (int i = 0; i < NB && i < gk; ++i) {
+        const int last = gk - 1 - ((gk - 1 - i) % NB);  // the last use of buffer i
+        wait_bar(&bfree[i], (uint32_t)((last / NB) & 1));
+      }
     }
   }
 
@@ -689,10 +822,13 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
   __syncwarp();
   tc::tc_fence_before();
   __syncthreads();
+  // pairs: neither CTA frees its TMEM or leaves while the other may still arrive on its barriers
+  if (CG == 2) tc::cluster_sync();
   if (warp == 1) {
     __syncwarp();
     tc::tc_fence_after();
-    tc::tmem_dealloc(tbase, C::TMEM_COLS);
+    if (CG == 2) tc::tmem_dealloc_pair(tbase, C::TMEM_COLS);
+    else tc::tmem_dealloc(tbase, C::TMEM_COLS);
   }
 }
 
@@ -700,22 +836,61 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB>::THREADS, 1)
 
 bool tma_ok_stride(int64_t s_elems, int esz) { return ((s_elems * esz) % 16) == 0; }
 
-template <int BN, bool BF16, int DEQ, int MSUB>
+template <int BN, bool BF16, int DEQ, int MSUB, int CG = 1>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc_, const TcParams& p, cudaStream_t st,
                   const char* name) {
-  using C = Cfg<BN, DEQ, MSUB>;
-  static bool attr_set = false;  // set once per process (single device per process)
+  using C = Cfg<BN, DEQ, MSUB, CG>;
+  auto kern = gemm_tc_kernel<BN, BF16, DEQ, MSUB, CG>;
+  static int max_pairs = 0;  // set once per process (single device per process)
+  static bool attr_set = false;
   if (!attr_set) {
-    if (int rc = check_cuda(cudaFuncSetAttribute(gemm_tc_kernel<BN, BF16, DEQ, MSUB>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                             "cudaFuncSetAttribute(gemm_tc)"))
       return rc;
+    if (CG == 2) {
+      // persistent grid: as many CTA pairs as the GPU can hold at once (one CTA per SM)
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * device_info().sm_count);
+      cfg.blockDim = dim3(C::THREADS);
+      cfg.dynamicSmemBytes = C::SMEM;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+      cfg.attrs = at, cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = device_info().sm_count / 2;
+      }
+      max_pairs = n;
+    }
     attr_set = true;
   }
-  int tiles = p.m_tiles * p.n_tiles * (int)p.batch * p.ksplit;
+  const int tiles = p.m_tiles * p.n_tiles * (int)p.batch * p.ksplit;
+  if (CG == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * std::min(tiles, max_pairs)));
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+    cfg.attrs = at, cfg.numAttrs = 1;
+    cudaError_t e;
+    {
+      LaunchScope ls(name, st);
+      e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_, p);
+    }
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail_cuda(e, name);
+    }
+    return after_launch(name);
+  }
   int grid = std::min(tiles, device_info().sm_count);
   LaunchScope ls(name, st);
-  gemm_tc_kernel<BN, BF16, DEQ, MSUB><<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, tc_, p);
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, tc_, p);
   return after_launch(name);
 }
 
@@ -964,12 +1139,20 @@ uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a) {
 // TMA-stored and summed (with the bias) by gemm_splitk_reduce. With K = 2048 the partial traffic and
 // the second kernel cost more than the split gains (measured 30 -> 45 us at 1024x2048x2048).
 struct Int8Plan {
-  int bn, msub, ksplit, kps;
+  int bn, msub, ksplit, kps, cg;
 };
 Int8Plan int8_plan(const b2_int8_gemm_args* a) {
-  struct Choice { int bn, msub; double eff; };
-  const Choice fwd_opts[] = {{256, 2, 1.15}, {176, 2, 1.08}, {128, 2, 1.0}, {96, 2, 0.97}, {256, 1, 0.85}, {128, 1, 0.55}};
-  const Choice dx_opts[] = {{256, 2, 1.15}, {128, 2, 1.0}, {256, 1, 0.85}, {128, 1, 0.55}};
+  // cg = 2: a CTA pair (cta_group::2) shares each MMA, every CTA staging and dequantising only half of
+  // the B tile, which halves the dequant work and the B operand bytes per CTA; pair tiles are
+  // 2 * 128 * msub rows by bn columns and use half as many units of GPU capacity (one per pair).
+  // eff: measured relative per-SM rate of each shape (pairs: estimated from their shared-memory bytes
+  // per K block until measured, B2_INT8_CG=1|2 pins the choice for sweeps).
+  struct Choice { int bn, msub, cg; double eff; };
+  const Choice fwd_opts[] = {{256, 2, 2, 1.55}, {176, 2, 2, 1.45}, {256, 1, 2, 1.3}, {128, 2, 2, 1.25},
+                             {256, 2, 1, 1.15}, {176, 2, 1, 1.08}, {128, 2, 1, 1.0},  {96, 2, 1, 0.97},
+                             {256, 1, 1, 0.85}, {128, 1, 1, 0.55}};
+  const Choice dx_opts[] = {{256, 2, 2, 1.55}, {256, 1, 2, 1.3}, {128, 2, 2, 1.25}, {256, 2, 1, 1.15},
+                            {128, 2, 1, 1.0},  {256, 1, 1, 0.85}, {128, 1, 1, 0.55}};
   const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
   const int64_t out_cols = a->transpose_w ? a->K : a->N;
   const int64_t red = a->transpose_w ? a->N : a->K;
@@ -979,30 +1162,43 @@ Int8Plan int8_plan(const b2_int8_gemm_args* a) {
     int bn = 0, ms = 0;
     return (e && sscanf(e, "%dx%d", &bn, &ms) == 2) ? bn * 10 + ms : 0;
   }();
-  Int8Plan best{0, 0, 1, k_blocks};
+  static const int forced_cg = [] {
+    const char* e = getenv("B2_INT8_CG");
+    return (e && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
+  }();
+  Int8Plan best{0, 0, 1, k_blocks, 1};
   double best_score = -1.0;
-  const int nopts = a->transpose_w ? 4 : 6;
+  const int nopts = a->transpose_w ? 7 : 10;
   for (int i = 0; i < nopts; ++i) {
     const Choice c = a->transpose_w ? dx_opts[i] : fwd_opts[i];
-    const int64_t tiles = ((a->M + 128 * c.msub - 1) / (128 * c.msub)) * ((out_cols + c.bn - 1) / c.bn);
-    const int64_t waves = (tiles + sms - 1) / sms;
-    double score = (double)a->M * out_cols / ((double)waves * sms * 128 * c.msub * c.bn) * c.eff;
-    if (forced) score = (forced == c.bn * 10 + c.msub) ? 1e9 : -1.0;
-    if (score > best_score) best_score = score, best = Int8Plan{c.bn, c.msub, 1, k_blocks};
+    if (forced_cg && c.cg != forced_cg) continue;
+    if (a->epilogue && c.bn % 32) continue;  // fused epilogues run on whole 32-column chunks
+    const int64_t rows = 128 * c.msub * c.cg, cap = sms / c.cg;
+    const int64_t tiles = ((a->M + rows - 1) / rows) * ((out_cols + c.bn - 1) / c.bn);
+    const int64_t waves = (tiles + cap - 1) / cap;
+    double score = (double)a->M * out_cols / ((double)waves * cap * rows * c.bn) * c.eff;
+    if (forced) score = (forced == c.bn * 10 + c.msub) ? 1e9 * c.eff : -1.0;
+    if (score > best_score) best_score = score, best = Int8Plan{c.bn, c.msub, 1, k_blocks, c.cg};
   }
-  if (best.bn == 0) best = Int8Plan{128, 2, 1, k_blocks};
-  // split-K over 256x256 tiles
-  const int64_t tiles = ((a->M + 255) / 256) * ((out_cols + 255) / 256);
-  if (!forced && a->workspace_bytes > 0 && tiles * 2 <= sms && k_blocks >= 64) {
-    const int want = (int)std::min<int64_t>(sms / tiles, k_blocks / 8);
-    if (want >= 2) {
+  if (best.bn == 0) best = Int8Plan{128, 2, 1, k_blocks, 1};
+  // split-K over 256x256 tiles (CTA pairs: 512x256) when too few tiles fill the GPU and K is long
+  if (!forced && !a->epilogue && a->workspace_bytes > 0 && k_blocks >= 64) {
+    for (int cg = 1; cg <= 2; ++cg) {
+      if (forced_cg && cg != forced_cg) continue;
+      const int64_t rows = 256 * cg, cap = sms / cg;
+      const double eff = cg == 2 ? 1.55 : 1.15;
+      const int64_t tiles = ((a->M + rows - 1) / rows) * ((out_cols + 255) / 256);
+      if (tiles * 2 > cap) continue;
+      const int want = (int)std::min<int64_t>(cap / tiles, k_blocks / 8);
+      if (want < 2) continue;
       const int kps = (k_blocks + want - 1) / want;
       const int ks = (k_blocks + kps - 1) / kps;
       const int64_t units = tiles * ks;
-      const int64_t waves = (units + sms - 1) / sms;
-      const double score = (double)a->M * out_cols / ((double)waves * sms * 256 * 256) * ks * 1.15 * 0.8;
+      const int64_t waves = (units + cap - 1) / cap;
+      const double score = (double)a->M * out_cols / ((double)waves * cap * rows * 256) * ks * eff * 0.8;
       const uint64_t need = (uint64_t)ks * a->M * out_cols * sizeof(float);
-      if (score > best_score && (uint64_t)a->workspace_bytes >= need) best = Int8Plan{256, 2, ks, kps};
+      if (score > best_score && (uint64_t)a->workspace_bytes >= need)
+        best_score = score, best = Int8Plan{256, 2, ks, kps, cg};
     }
   }
   return best;
@@ -1027,15 +1223,19 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   if (((uintptr_t)a->x & 15) || ((uintptr_t)a->q & 15) || a->x_ld % 8 || a->K % 16)
     return fail(B2_ERR_ARG, "int8_gemm: x and q must be 16-byte aligned, x_ld a multiple of 8 and K of 16");
   if (a->transpose_w && a->bias) return fail(B2_ERR_ARG, "int8_gemm: bias is only supported in the forward form");
+  if (a->epilogue < 0 || a->epilogue > 2 || (a->epilogue == 1 && a->transpose_w) || (a->epilogue == 2 && !a->transpose_w))
+    return fail(B2_ERR_ARG, "int8_gemm: epilogue 1 (GELU) needs the forward form, 2 (GELU backward) the transposed form");
+  if (a->epilogue && (!a->aux || ((uintptr_t)a->aux & 15) || a->aux_ld < out_cols || a->aux_ld % 8))
+    return fail(B2_ERR_ARG, "int8_gemm: the GELU epilogue needs a 16-byte aligned bf16 aux with aux_ld >= out_cols, a multiple of 8");
   cudaStream_t st = (cudaStream_t)stream;
   if (a->workspace && ((uintptr_t)a->workspace & 15)) return fail(B2_ERR_ARG, "int8_gemm: workspace must be 16-byte aligned");
   b2_int8_gemm_args aa = *a;
   if (!aa.workspace) aa.workspace_bytes = 0;
   const Int8Plan best = int8_plan(&aa);
-  const int BN = best.bn, BMT = 128 * best.msub;
+  const int BN = best.bn, BMT = 128 * best.msub, BNC = best.bn / best.cg;
   TcParams p{};
   p.M = a->M, p.N = out_cols, p.K = red, p.batch = 1;
-  p.m_tiles = (int)((a->M + BMT - 1) / BMT);
+  p.m_tiles = (int)((a->M + BMT * best.cg - 1) / (BMT * best.cg));
   p.n_tiles = (int)((out_cols + BN - 1) / BN);
   p.k_blocks = (int)((red + BK - 1) / BK);
   p.a_mn = 0;
@@ -1050,6 +1250,9 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   setup_cmap(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p);
+  p.epi = a->epilogue, p.aux = a->aux, p.aux_ld = a->aux_ld;
+  if (p.epi && p.c_tma != 1)
+    return fail(B2_ERR_ARG, "int8_gemm: the GELU epilogue needs an output a tensor map can describe (16-byte rows)");
   CUtensorMap ta, tb;
   {
     uint64_t dims[2] = {(uint64_t)red, (uint64_t)a->M}, strides[1] = {(uint64_t)a->x_ld * 2};
@@ -1060,14 +1263,20 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   {
     uint64_t dims[2] = {(uint64_t)a->K, (uint64_t)a->N}, strides[1] = {(uint64_t)a->K};
     uint32_t box[2];
-    if (!a->transpose_w) box[0] = 64, box[1] = (uint32_t)BN;
-    else box[0] = (uint32_t)BN, box[1] = 64;
+    if (!a->transpose_w) box[0] = 64, box[1] = (uint32_t)BNC;  // each CTA of a pair loads its half
+    else box[0] = (uint32_t)BNC, box[1] = 64;
     if (!make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
       return fail(B2_ERR_ARG, "int8_gemm: tensor map for q rejected");
   }
   const char* name = a->transpose_w ? "int8_gemm_dx" : "int8_gemm_fwd";
   int rc;
-  if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name);
+  if (best.cg == 2) {
+    const char* pname = a->transpose_w ? "int8_gemm_dx_pair" : "int8_gemm_fwd_pair";
+    if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2, 2>(ta, tb, tcm, p, st, pname);
+    else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2, 2>(ta, tb, tcm, p, st, pname);
+    else if (best.msub == 2) rc = launch_kernel<128, true, 2, 2, 2>(ta, tb, tcm, p, st, pname);
+    else rc = launch_kernel<256, true, 2, 1, 2>(ta, tb, tcm, p, st, pname);
+  } else if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name);
   else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name);
   else if (best.msub == 2 && BN == 128) rc = launch_kernel<128, true, 2, 2>(ta, tb, tcm, p, st, name);
   else if (best.msub == 2 && BN == 96) rc = launch_kernel<96, true, 2, 2>(ta, tb, tcm, p, st, name);

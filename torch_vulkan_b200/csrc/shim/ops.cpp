@@ -628,9 +628,10 @@ at::Tensor int8_workspace(b2_int8_gemm_args& g, const at::Tensor& like) {
   return ws;
 }
 
-// y[..., N] = x[..., K] @ (q * scale)^T + bias
-at::Tensor b2_int8_linear_fwd(const at::Tensor& x0, const at::Tensor& q, const at::Tensor& scale0,
-                              const std::optional<at::Tensor>& bias0) {
+// y[..., N] = x[..., K] @ (q * scale)^T + bias; with `gelu_out` the GEMM's epilogue also writes
+// gelu_tanh(y) there (the DiT MLP's fc1: y is the pre-activation the backward needs)
+at::Tensor int8_fwd_impl(const at::Tensor& x0, const at::Tensor& q, const at::Tensor& scale0,
+                         const std::optional<at::Tensor>& bias0, at::Tensor* gelu_out) {
   TORCH_CHECK(x0.is_cuda() && q.is_cuda(), "int8_linear: CUDA tensors required");
   TORCH_CHECK(x0.scalar_type() == at::kBFloat16, "int8_linear: x must be bfloat16");
   TORCH_CHECK(q.scalar_type() == at::kChar && q.dim() == 2 && q.is_contiguous(), "int8_linear: q must be contiguous int8 [N,K]");
@@ -644,7 +645,11 @@ at::Tensor b2_int8_linear_fwd(const at::Tensor& x0, const at::Tensor& q, const a
   std::vector<int64_t> osz(x0.sizes().begin(), x0.sizes().end());
   osz.back() = N;
   at::Tensor out = at::empty({x.size(0), N}, x.options());
-  if (out.numel() == 0) return out.view(osz);
+  if (gelu_out) *gelu_out = at::empty({x.size(0), N}, x.options());
+  if (out.numel() == 0) {
+    if (gelu_out) *gelu_out = gelu_out->view(osz);
+    return out.view(osz);
+  }
   at::Tensor bias;
   if (bias0.has_value() && bias0->defined()) {
     bias = bias0->contiguous();
@@ -657,14 +662,31 @@ at::Tensor b2_int8_linear_fwd(const at::Tensor& x0, const at::Tensor& q, const a
   g.M = x.size(0), g.N = N, g.K = K, g.x_ld = K, g.out_ld = N;
   g.scale_layout = layout;
   g.transpose_w = 0;
+  if (gelu_out) g.epilogue = 1, g.aux = gelu_out->data_ptr(), g.aux_ld = N;
   at::Tensor ws = int8_workspace(g, x);
-  b2_check(b2_int8_gemm(&g, cur_stream()), "int8_linear_fwd");
-  count("b2::int8_linear");
+  b2_check(b2_int8_gemm(&g, cur_stream()), gelu_out ? "int8_linear_gelu_fwd" : "int8_linear_fwd");
+  count(gelu_out ? "b2::int8_linear_gelu" : "b2::int8_linear");
+  if (gelu_out) *gelu_out = gelu_out->view(osz);
   return out.view(osz);
 }
 
-// dx[..., K] = dy[..., N] @ (q * scale)
-at::Tensor b2_int8_linear_dx(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0) {
+at::Tensor b2_int8_linear_fwd(const at::Tensor& x0, const at::Tensor& q, const at::Tensor& scale0,
+                              const std::optional<at::Tensor>& bias0) {
+  return int8_fwd_impl(x0, q, scale0, bias0, nullptr);
+}
+
+// (gelu_tanh(h), h) with h = x @ (q * scale)^T + bias, from one GEMM
+std::tuple<at::Tensor, at::Tensor> b2_int8_linear_gelu_fwd(const at::Tensor& x0, const at::Tensor& q,
+                                                           const at::Tensor& scale0,
+                                                           const std::optional<at::Tensor>& bias0) {
+  at::Tensor act;
+  at::Tensor h = int8_fwd_impl(x0, q, scale0, bias0, &act);
+  return {act, h};
+}
+
+// dx[..., K] = dy[..., N] @ (q * scale); with `h` (the pre-activation of a GELU that follows this
+// linear's input) the epilogue returns dx * gelu_tanh'(h) instead
+at::Tensor int8_dx_impl(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0, const at::Tensor* h) {
   TORCH_CHECK(dy0.is_cuda() && q.is_cuda() && dy0.scalar_type() == at::kBFloat16, "int8_linear_dx: bf16 CUDA dy required");
   c10::cuda::CUDAGuard guard(dy0.device());
   const int64_t N = q.size(0), K = q.size(1);
@@ -676,16 +698,33 @@ at::Tensor b2_int8_linear_dx(const at::Tensor& dy0, const at::Tensor& q, const a
   osz.back() = K;
   at::Tensor dx = at::empty({dy.size(0), K}, dy.options());
   if (dx.numel() == 0) return dx.view(osz);
+  at::Tensor hh;
+  if (h) {
+    TORCH_CHECK(h->scalar_type() == at::kBFloat16 && h->numel() == dx.numel() && h->size(-1) == K,
+                "int8_linear_dx_gelu: h must be bf16 with the shape of dx");
+    hh = h->reshape({-1, K});
+    if (!hh.is_contiguous()) hh = hh.contiguous();
+  }
   b2_int8_gemm_args g{};
   g.x = dy.data_ptr(), g.q = (const int8_t*)q.data_ptr(), g.scale = scale.data_ptr();
   g.out = dx.data_ptr();
   g.M = dy.size(0), g.N = N, g.K = K, g.x_ld = N, g.out_ld = K;
   g.scale_layout = layout;
   g.transpose_w = 1;
+  if (h) g.epilogue = 2, g.aux = hh.data_ptr(), g.aux_ld = K;
   at::Tensor ws = int8_workspace(g, dy);
-  b2_check(b2_int8_gemm(&g, cur_stream()), "int8_linear_dx");
-  count("b2::int8_linear_dx");
+  b2_check(b2_int8_gemm(&g, cur_stream()), h ? "int8_linear_dx_gelu" : "int8_linear_dx");
+  count(h ? "b2::int8_linear_dx_gelu" : "b2::int8_linear_dx");
   return dx.view(osz);
+}
+
+at::Tensor b2_int8_linear_dx(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0) {
+  return int8_dx_impl(dy0, q, scale0, nullptr);
+}
+
+at::Tensor b2_int8_linear_dx_gelu(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0,
+                                  const at::Tensor& h) {
+  return int8_dx_impl(dy0, q, scale0, &h);
 }
 
 // One AdamW step for a list of parameters (the arithmetic and roundings of torch.optim.AdamW with
@@ -792,6 +831,8 @@ TORCH_LIBRARY(b2, m) {
   m.def("dequant_int8(Tensor q, Tensor scale, ScalarType out_dtype) -> Tensor");
   m.def("int8_linear_fwd(Tensor x, Tensor q, Tensor scale, Tensor? bias) -> Tensor");
   m.def("int8_linear_dx(Tensor dy, Tensor q, Tensor scale) -> Tensor");
+  m.def("int8_linear_gelu_fwd(Tensor x, Tensor q, Tensor scale, Tensor? bias) -> (Tensor, Tensor)");
+  m.def("int8_linear_dx_gelu(Tensor dy, Tensor q, Tensor scale, Tensor h) -> Tensor");
   m.def("adamw_step_(Tensor(a!)[] params, Tensor[] grads, Tensor(b!)[] exp_avgs, Tensor(c!)[] exp_avg_sqs, float lr, "
         "float beta1, float beta2, float eps, float weight_decay, int step) -> ()");
   m.def("set_enabled(bool on) -> ()", &op_set_enabled);
@@ -806,5 +847,7 @@ TORCH_LIBRARY_IMPL(b2, CUDA, m) {
   m.impl("dequant_int8", &b2_dequant_int8_op);
   m.impl("int8_linear_fwd", &b2_int8_linear_fwd);
   m.impl("int8_linear_dx", &b2_int8_linear_dx);
+  m.impl("int8_linear_gelu_fwd", &b2_int8_linear_gelu_fwd);
+  m.impl("int8_linear_dx_gelu", &b2_int8_linear_dx_gelu);
   m.impl("adamw_step_", &b2_adamw_step_op);
 }

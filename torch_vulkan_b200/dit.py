@@ -139,7 +139,9 @@ class DiTBlock(nn.Module):
         h = modln(x, sh2, sc2)
         x = torch.addcmul(x, g2, self._attn(h, text, text, self.cq, self.ck, self.cv, self.co))
         h = modln(x, sh3, sc3)
-        x = torch.addcmul(x, g3, self.fc2(F.gelu(self.fc1(h), approximate="tanh")))
+        # MLP fc2(gelu(fc1(h))) with the GELU (and its backward) in the int8 GEMM epilogues
+        mlp = tv.int8_mlp(h, self.fc1.q, self.fc1.scale, self.fc1.bias, self.fc2.q, self.fc2.scale, self.fc2.bias)
+        x = torch.addcmul(x, g3, mlp)
         return x
 
 
@@ -209,11 +211,13 @@ class LoRATrainer:
         return loss.detach()
 
     def graphed(self, x, text, cond, target, warmup=3):
-        """Single-process step with forward + backward captured once as a CUDA graph (the inputs are the
-        graph's static buffers: copy new data into them before each call) and the optimizer launched
-        after each replay. Returns a callable performing one step and returning the loss tensor."""
-        if self.reducer.world > 1:
-            raise RuntimeError("graphed(): single process only (the all-reduce hooks run on the host)")
+        """Step with forward + backward captured once as a CUDA graph (the inputs are the graph's static
+        buffers: copy new data into them before each call) and the optimizer launched after each replay.
+        With several ranks the bucket all-reduces that the gradient hooks launch during the captured
+        backward are captured too (NCCL collectives replay inside the graph, still overlapping the
+        backward of earlier blocks); every rank captures the same collectives in the same order. Warm-up
+        steps run first so that NCCL's communicators exist before the capture. Returns a callable
+        performing one step and returning the loss tensor."""
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -222,12 +226,14 @@ class LoRATrainer:
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
+        self.reducer.zero_grad()  # re-arm the hooks so the captured backward launches every bucket
         with torch.cuda.graph(graph):
             for flat in self.reducer.flats:  # gradients accumulate into the bucket buffers
                 flat.zero_()
             loss = F.mse_loss(self.model(x, text, cond).float(), target.float())
             loss.backward()
-        self._graph = graph  # kept alive with its memory pool
+            self.reducer.wait()  # the captured collectives join the capture stream before it ends
+        self._graph = graph  # kept alive with its memory pool (release it before destroying the group)
 
         def run():
             graph.replay()
