@@ -61,7 +61,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--no-dit", action="store_true")
-    ap.add_argument("--case", choices=["attn", "int8", "rows", "dit"], default=None,
+    ap.add_argument("--case", choices=["attn", "attn4k", "attn_cross", "gemm", "gemm_dit", "int8", "rows", "dit"],
+                    default=None,
                     help="run a few eager iterations of one workload and exit (the small case for ncu captures)")
     ap.add_argument("--case-iters", type=int, default=3)
     return ap.parse_args()
@@ -400,9 +401,16 @@ def run_dit(dev, world, blocks, tokens, steps, warmup):
     model = DiTStack(blocks=blocks, seed=0, device=dev)  # identical replicas on every rank
     trainer = LoRATrainer(model, lr=1e-4, fused_optimizer=True)
     batch = synthetic_batch(tokens=tokens, seed=1000 + rank, device=dev)  # each rank its own sample
-    # forward + backward (with the bucketed NCCL all-reduces the gradient hooks launch, when N > 1)
-    # replayed as one CUDA graph per rank, optimizer launched after each replay
-    step = trainer.graphed(*batch, warmup=warmup)
+    # forward + backward (with the bucketed NCCL all-reduces the gradient hooks launch, when N > 1) replayed
+    # as one CUDA graph per rank, optimizer launched after each replay; if the capture is refused the step
+    # runs eagerly (every rank takes the same branch: the capture fails or succeeds alike everywhere)
+    graphed = True
+    try:
+        step = trainer.graphed(*batch, warmup=warmup)
+    except RuntimeError as e:
+        print(f"bench: graphed DiT step unavailable ({e}); timing the eager step", file=sys.stderr)
+        graphed = False
+        step = lambda: trainer.step(*batch)  # noqa: E731
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
@@ -425,7 +433,8 @@ def run_dit(dev, world, blocks, tokens, steps, warmup):
            "loss": float(loss.item()), "lora_params": sum(p.numel() for p in trainer.params),
            "allreduce": "bucketed per block, NCCL AVG, overlapped with backward" if world > 1 else None,
            "optimizer": "multi-tensor AdamW kernel (the arithmetic of AdamW foreach=False)",
-           "timing": "CUDA graph of forward + backward" + (" + bucketed NCCL all-reduces" if world > 1 else "") + ", optimizer after each replay"}
+           "timing": ("CUDA graph of forward + backward" + (" + bucketed NCCL all-reduces" if world > 1 else "") +
+                      ", optimizer after each replay") if graphed else "eager"}
     del trainer, model
     torch.cuda.empty_cache()
     return out
@@ -665,10 +674,27 @@ def run_case(name, iters):
 
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(0)
-    if name == "attn":
-        q, k, v, do = (t.to(dev) for t in make_inputs())
+    if name in ("attn", "attn4k", "attn_cross"):
+        # configs[1]; configs[4]'s self-attention (S = 4096) and its cross-attention (4096 x 512 text tokens)
+        sq, sk = {"attn": (S, S), "attn4k": (4096, 4096), "attn_cross": (4096, 512)}[name]
+        mk = lambda s_: torch.randn(B, H, s_, D, generator=g).to(torch.bfloat16).to(dev)  # noqa: E731
+        q, k, v, do = mk(sq), mk(sk), mk(sk), mk(sq)
         q.requires_grad_(True), k.requires_grad_(True), v.requires_grad_(True)
         fn = lambda: torch.autograd.grad(F.scaled_dot_product_attention(q, k, v), (q, k, v), do)  # noqa: E731
+    elif name in ("gemm", "gemm_dit"):
+        # bf16 tcgen05 GEMM: 8192^3, or the DiT block's LoRA projections (skinny, split-K) at 4096 tokens
+        if name == "gemm":
+            a, b = (torch.randn(8192, 8192, generator=g).to(torch.bfloat16).to(dev) for _ in range(2))
+            fn = lambda: torch.mm(a, b)  # noqa: E731
+        else:
+            x = torch.randn(4096, 2048, generator=g).to(torch.bfloat16).to(dev)
+            w_down = torch.randn(48, 2048, generator=g).to(torch.bfloat16).to(dev)
+            w_up = torch.randn(6144, 48, generator=g).to(torch.bfloat16).to(dev)
+            y = torch.randn(4096, 6144, generator=g).to(torch.bfloat16).to(dev)
+
+            def fn():
+                h = torch.nn.functional.linear(x, w_down)
+                torch.addmm(y, h, w_up.t())
     elif name == "int8":
         x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
         qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8).to(dev)

@@ -237,6 +237,16 @@ typedef struct b2_int8_gemm_args {
   int32_t pad_;
   void* aux;
   int64_t aux_ld;
+  /* LoRA side path added by the same GEMM as one extra 64-wide reduction block (new; the reference
+   * runs it as separate linears, tests/anima_on_vk.py:43-48). lora_r (8..64, a multiple of 8) = 0: none.
+   *   forward form:    out += lora_h[M, r] @ lora_b[N, r]^T  (lora_h = x @ A^T, lora_b = B * alpha / r)
+   *   transposed form: out += lora_h[M, r] @ lora_b[r, K]    (lora_h = dY @ B * alpha / r, lora_b = A)
+   * bf16, rows 16-byte aligned with leading dims lora_h_ld / lora_b_ld (multiples of 8). No split-K. */
+  const void* lora_h;
+  const void* lora_b;
+  int64_t lora_h_ld, lora_b_ld;
+  int32_t lora_r;
+  int32_t pad2_;
 } b2_int8_gemm_args;
 int b2_int8_gemm(const b2_int8_gemm_args* args, b2_stream_t stream);
 uint64_t b2_int8_gemm_workspace_bytes(const b2_int8_gemm_args* args);

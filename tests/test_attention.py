@@ -141,3 +141,48 @@ def test_config2_attention_and_tc_vs_simt(tv):
         tv.set_tc_attention_enabled(True)
     for a, b in zip(got, simt):
         assert rel_err(a, b) < 2e-2
+
+
+PAIR_CHILD = r"""
+import json, sys
+sys.path.insert(0, ROOT)
+import torch
+import oracle
+import torch_vulkan_b200 as tv
+
+OVR = torch.ops.aten._scaled_dot_product_fused_attention_overrideable
+g = torch.Generator().manual_seed(11)
+out = []
+tv.profile_enable(True)
+for B, H, Sq, Sk, dt in [(1, 16, 1024, 1024, torch.bfloat16), (1, 2, 4096, 512, torch.bfloat16),
+                         (2, 3, 300, 200, torch.float16), (1, 2, 129, 77, torch.bfloat16)]:
+    q, k, v = (torch.randn(B, H, S, 128, generator=g).to(dt) for S in (Sq, Sk, Sk))
+    o, lse = OVR(q.cuda(), k.cuda(), v.cuda())[:2]
+    o64, lse64 = oracle.sdpa_fwd(q, k, v)
+    e = ((o.cpu().double() - o64).norm() / o64.norm()).item()
+    le = (lse.cpu().double() - lse64).abs().max().item() / max(1.0, lse64.abs().max().item())
+    out.append([B, H, Sq, Sk, str(dt), e, le])
+torch.cuda.synchronize()
+kernels = [ln.split("\t")[0] for ln in tv.profile().splitlines() if ln]
+print("RESULT " + json.dumps({"cases": out, "kernels": kernels, "validation_errors": tv.validation_errors()}))
+"""
+
+
+def test_pair_forward_opt_in_matches_oracle():
+    """The CTA-pair forward (B2_ATTN_FWD_PAIRS=1, D = 128): O and logsumexp against the float64 oracle at the
+    config-2 shape, a 4096 x 512 cross-attention and ragged query/key counts (odd tile counts leave the
+    second CTA of the last pair without rows)."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", PAIR_CHILD.replace("ROOT", repr(root))], capture_output=True,
+                       text=True, timeout=600, cwd=root, env=dict(os.environ, B2_ATTN_FWD_PAIRS="1"))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("RESULT ")][-1][len("RESULT "):])
+    assert res["validation_errors"] == 0
+    assert "attn_fwd_tc_pair" in res["kernels"], res["kernels"]
+    for B, H, Sq, Sk, dt, e, le in res["cases"]:
+        assert e < 2e-2 and le <= 1e-3, (B, H, Sq, Sk, dt, e, le)

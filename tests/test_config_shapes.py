@@ -33,7 +33,9 @@ class Int8Args(ctypes.Structure):
                 ("out", ctypes.c_void_p), ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
                 ("x_ld", ctypes.c_int64), ("out_ld", ctypes.c_int64), ("scale_layout", ctypes.c_int32),
                 ("transpose_w", ctypes.c_int32), ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
-                ("epilogue", ctypes.c_int32), ("pad_", ctypes.c_int32), ("aux", ctypes.c_void_p), ("aux_ld", ctypes.c_int64)]
+                ("epilogue", ctypes.c_int32), ("pad_", ctypes.c_int32), ("aux", ctypes.c_void_p), ("aux_ld", ctypes.c_int64),
+                ("lora_h", ctypes.c_void_p), ("lora_b", ctypes.c_void_p), ("lora_h_ld", ctypes.c_int64),
+                ("lora_b_ld", ctypes.c_int64), ("lora_r", ctypes.c_int32), ("pad2_", ctypes.c_int32)]
 
 
 @pytest.fixture(scope="module")

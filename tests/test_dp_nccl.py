@@ -104,10 +104,16 @@ def _spawn(target, world=2):
     procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=300) for _ in range(world)]
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    try:
+        out = [q.get(timeout=240) for _ in range(world)]
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    finally:  # a rank that failed must not outlive the test (its peer would wait in NCCL)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     return {o[0]: o[1:] for o in out}
 
 

@@ -294,6 +294,40 @@ def int8_linear(x: torch.Tensor, q: torch.Tensor, scale: torch.Tensor, bias: tor
     return _Int8Linear.apply(x, q, scale, bias)
 
 
+class _Int8LoRA(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, q, scale, bias, a, b):
+        x2 = x.reshape(-1, x.shape[-1])
+        h = torch.mm(x2, a.t())  # the rank-r down-projection
+        y = torch.ops.b2.int8_lora_fwd(x2, q, scale, bias, h, b)  # base + bias + h b^T in one GEMM
+        ctx.save_for_backward(x2, q, scale, a, b, h)
+        ctx.x_shape = x.shape
+        ctx.has_bias = bias is not None
+        return y.view(*x.shape[:-1], q.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, q, scale, a, b, h = ctx.saved_tensors
+        gy2 = gy.reshape(-1, gy.shape[-1]).contiguous()
+        dh = torch.mm(gy2, b)  # [rows, r]
+        gx = None
+        if ctx.needs_input_grad[0]:  # dy @ W~ + dh @ A in one GEMM
+            gx = torch.ops.b2.int8_lora_dx(gy2, q, scale, dh, a).view(ctx.x_shape)
+        ga = torch.mm(dh.t(), x2) if ctx.needs_input_grad[4] else None
+        gb = torch.mm(gy2.t(), h) if ctx.needs_input_grad[5] else None
+        gbias = gy2.sum(0) if (ctx.has_bias and ctx.needs_input_grad[3]) else None
+        return gx, None, None, gbias, ga, gb
+
+
+def int8_lora_linear(x, q, scale, bias, a, b):
+    """y = x @ (q * scale)^T + bias + (x @ a^T) @ b^T — a frozen int8 linear with its LoRA side path, where
+    a [r, K] is the down-projection and b [N, r] the up-projection already multiplied by alpha / r (r a
+    multiple of 8, at most 64; stacked modules pass their concatenated down-projections and block-diagonal
+    up-projections). The up-projection is one more 64-wide reduction block of the int8 GEMM, and in the
+    backward dX = dY @ W~ + (dY @ b) @ a is one GEMM too. Differentiable in x, a, b (and bias)."""
+    return _Int8LoRA.apply(x, q, scale, bias, a, b)
+
+
 class _Int8GeluMLP(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, q1, s1, b1, q2, s2, b2):

@@ -18,6 +18,7 @@
 //           converted at the end.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code and unwinds.
 #include <cuda.h>
+#include <cstdlib>
 #include <cstring>
 
 #include <type_traits>
@@ -67,14 +68,21 @@ struct AttnTcParams {
 // ==================================================================================================
 // forward: two softmax warpgroups split the KV blocks (even / odd), each with its own TMEM S and O
 // ==================================================================================================
-template <int D>
+// CG = 2: a cluster pair of CTAs shares every MMA (tcgen05 cta_group::2, M = 256 query rows, 128 per
+// CTA): each CTA stages its own Q rows but only half of each K block (64 keys) and half of each V block
+// (64 of the 128 head-dim columns), which halves the per-CTA K/V traffic into shared memory and the
+// B-operand reads of both MMAs. The leader (even CTA) issues the MMAs for both.
+template <int D, int CG = 1>
 struct FwdCfg {
   static constexpr int BQ = 128, BKV = 128;
   static constexpr int DCH = D / 64;                 // 64-element chunks along D
+  static constexpr int KROWS = BKV / CG;              // keys of a K block this CTA stages
+  static constexpr int VCH = DCH / CG;                // 64-column V chunks this CTA stages
+  static_assert(CG == 1 || D == 128, "CTA pairs split V by 64-column chunks: D = 128");
   static constexpr int Q_BYTES = BQ * D * 2;
-  static constexpr int K_BYTES = BKV * D * 2;
-  static constexpr int V_BYTES = BKV * D * 2;
-  static constexpr int NS = 3;                        // K / V ring depth
+  static constexpr int K_BYTES = KROWS * D * 2;
+  static constexpr int V_BYTES = BKV * 64 * VCH * 2;
+  static constexpr int NS = CG == 2 ? 4 : 3;          // K / V ring depth
   static constexpr int OFF_Q = 0;                     // also the (m, l) exchange area of the epilogue
   static constexpr int OFF_K = OFF_Q + Q_BYTES;       // NS stages
   static constexpr int OFF_V = OFF_K + NS * K_BYTES;  // NS stages
@@ -88,11 +96,11 @@ struct FwdCfg {
   static constexpr uint32_t T_S = 0, T_O = 256, TMEM_COLS = 512;
 };
 
-template <int D, bool BF16>
+template <int D, bool BF16, int CG>
 __global__ void __launch_bounds__(320, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, AttnTcParams p) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -109,10 +117,16 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(o_upd + 3);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * C::BQ;
+  // pairs: CTA rank r of the cluster takes query rows [q0, q0 + 128) of the pair's 256
+  const uint32_t rank = CG == 2 ? tc::cluster_ctarank() : 0u;
+  const int q0 = (int)(blockIdx.x / CG) * C::BQ * CG + (int)rank * C::BQ;
   const int bh = blockIdx.y;
   const int b = bh / (int)p.H, h = bh % (int)p.H;
   const int nblk = (int)((p.Sk + C::BKV - 1) / C::BKV);
+  // the leader's copy of a barrier (the barrier itself for single CTAs)
+  auto leader_bar = [&](uint64_t* bar) -> uint32_t {
+    return CG == 2 ? tc::mapa_shared(tc::smem_u32(bar), 0u) : tc::smem_u32(bar);
+  };
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
@@ -124,18 +138,24 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&p_full[i], 128);
+      tc::mbar_init(&p_full[i], CG == 2 ? 4 * CG : 128);  // pairs: one arrival per softmax warp
       tc::mbar_init(&o_upd[i], 1);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
+  if (CG == 2) tc::cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
   // the previous kernel on the stream must be done before any global or tensor memory is touched;
   // TMEM is allocated only after this wait, so a waiting CTA never holds columns another CTA needs
   tc::pdl_wait();
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tc::tmem_relinquish();
+    if (CG == 2) {
+      tc::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -146,25 +166,46 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- producer: Q once, then K_j / V_j into NS-stage rings ----------------
+      // pairs: every load lands in this CTA's shared memory and completes on the leader's barrier,
+      // which the leader arms for both CTAs' bytes
       bool ok = true;
-      tc::mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-      for (int c = 0; c < C::DCH; ++c) tc::tma_load_4d(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, q_full, c * 64, q0, h, b);
+      if (rank == 0) tc::mbar_arrive_expect_tx(q_full, C::Q_BYTES * CG);
+      for (int c = 0; c < C::DCH; ++c) {
+        if (CG == 2) tc::tma_load_4d_pair(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, leader_bar(q_full), c * 64, q0, h, b);
+        else tc::tma_load_4d(smem + C::OFF_Q + c * (C::BQ * 128), &tmQ, q_full, c * 64, q0, h, b);
+      }
       int issued_k[NS] = {}, issued_v[NS] = {};
       for (int j = 0; j < nblk && ok; ++j) {
         const int s = j % NS;
         const uint32_t ph = (uint32_t)((j / NS) & 1);
         if (!tc::mbar_wait(&k_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
-        tc::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES);
-        for (int c = 0; c < C::DCH; ++c)
-          tc::tma_load_4d(smem + C::OFF_K + s * C::K_BYTES + c * (C::BKV * 128), &tmK, &k_full[s], c * 64, j * C::BKV, h, b);
+        if (rank == 0) tc::mbar_arrive_expect_tx(&k_full[s], C::K_BYTES * CG);
+        for (int c = 0; c < C::DCH; ++c) {  // this CTA's keys of block j, all D columns
+          uint8_t* dst = smem + C::OFF_K + s * C::K_BYTES + c * (C::KROWS * 128);
+          const int krow = j * C::BKV + (int)rank * C::KROWS;
+          if (CG == 2) tc::tma_load_4d_pair(dst, &tmK, leader_bar(&k_full[s]), c * 64, krow, h, b);
+          else tc::tma_load_4d(dst, &tmK, &k_full[s], c * 64, krow, h, b);
+        }
         issued_k[s]++;
         if (!tc::mbar_wait(&v_empty[s], ph ^ 1, p.err) || *abort_flag) { ok = false; break; }
-        tc::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES);
-        for (int c = 0; c < C::DCH; ++c)
-          tc::tma_load_4d(smem + C::OFF_V + s * C::V_BYTES + c * (C::BKV * 128), &tmV, &v_full[s], c * 64, j * C::BKV, h, b);
+        if (rank == 0) tc::mbar_arrive_expect_tx(&v_full[s], C::V_BYTES * CG);
+        for (int c = 0; c < C::VCH; ++c) {  // all keys of block j, this CTA's 64-column V chunks
+          uint8_t* dst = smem + C::OFF_V + s * C::V_BYTES + c * (C::BKV * 128);
+          const int vcol = ((int)rank * C::VCH + c) * 64;
+          if (CG == 2) tc::tma_load_4d_pair(dst, &tmV, leader_bar(&v_full[s]), vcol, j * C::BKV, h, b);
+          else tc::tma_load_4d(dst, &tmV, &v_full[s], vcol, j * C::BKV, h, b);
+        }
         issued_v[s]++;
       }
-      if (!ok) {
+      if (ok && CG == 2) {
+        // pairs: the leader's last commits arrive on this CTA's empty barriers; wait for them before
+        // the CTA can leave
+        for (int s = 0; s < NS; ++s) {
+          if (issued_k[s]) tc::mbar_wait(&k_empty[s], (uint32_t)((issued_k[s] - 1) & 1), p.err);
+          if (issued_v[s]) tc::mbar_wait(&v_empty[s], (uint32_t)((issued_v[s] - 1) & 1), p.err);
+        }
+      }
+      if (!ok && rank == 0) {
         *abort_flag = 1;
         tc::mbar_wait(q_full, 0, nullptr);
         for (int s = 0; s < NS; ++s) {
@@ -174,13 +215,13 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (pairs: the leader only) ----------------
       // S_j = Q K_j^T into S[j&1]; once the softmax has replaced S_j by P_j (bf16, in TMEM),
       // O[j&1] += P_j V_j with A read from TMEM, then S_j+2 into the same columns: tcgen05.mma from
       // one thread executes in order, so S_j+2 cannot overwrite P_j before PV_j has read it.
-      constexpr uint32_t IDESC_S = tc::idesc_f16(128, C::BKV, BF16, false, false);  // Q K^T: both K-major
-      constexpr uint32_t IDESC_O = tc::idesc_f16(128, D, BF16, false, true);        // P V: V is MN-major
+      constexpr uint32_t IDESC_S = tc::idesc_f16(128 * CG, C::BKV, BF16, false, false);  // Q K^T: both K-major
+      constexpr uint32_t IDESC_O = tc::idesc_f16(128 * CG, D, BF16, false, true);        // P V: V is MN-major
       const tc::SDesc qd = tc::sdesc_parts(tc::smem_u32(smem + C::OFF_Q), 16, 1024);
       bool ok = tc::mbar_wait(q_full, 0, p.err);
       auto issue_s = [&](int j) -> bool {
@@ -191,11 +232,17 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t dst = tbase + C::T_S + s * 128;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * (128 * 128) + (k & 3) * 32;
-          tc::mma_f16_ss(dst, tc::sdesc_at(qd, off), tc::sdesc_at(kd, off), IDESC_S, k > 0 ? 1u : 0u);
+          const uint32_t qoff = (k >> 2) * (C::BQ * 128) + (k & 3) * 32, koff = (k >> 2) * (C::KROWS * 128) + (k & 3) * 32;
+          if (CG == 2) tc::mma_f16_ss_pair(dst, tc::sdesc_at(qd, qoff), tc::sdesc_at(kd, koff), IDESC_S, k > 0 ? 1u : 0u);
+          else tc::mma_f16_ss(dst, tc::sdesc_at(qd, qoff), tc::sdesc_at(kd, koff), IDESC_S, k > 0 ? 1u : 0u);
         }
-        tc::mma_commit(&s_full[s]);
-        tc::mma_commit(&k_empty[ks]);
+        if (CG == 2) {  // the S tile is ready in both CTAs; both CTAs' K stages are free
+          tc::mma_commit_pair(&s_full[s], (uint16_t)3);
+          tc::mma_commit_pair(&k_empty[ks], (uint16_t)3);
+        } else {
+          tc::mma_commit(&s_full[s]);
+          tc::mma_commit(&k_empty[ks]);
+        }
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -212,10 +259,17 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t o_dst = tbase + C::T_O + s * 128, p_src = tbase + C::T_S + s * 128;
         const uint32_t acc0 = j >= 2 ? 1u : 0u;
 #pragma unroll
-        for (int k = 0; k < C::BKV / 16; ++k)
-          tc::mma_f16_ts(o_dst, p_src + k * 8, tc::sdesc_at(vd, k * 2048), IDESC_O, k > 0 ? 1u : acc0);
-        tc::mma_commit(&o_upd[s]);
-        tc::mma_commit(&v_empty[ks]);
+        for (int k = 0; k < C::BKV / 16; ++k) {
+          if (CG == 2) tc::mma_f16_ts_pair(o_dst, p_src + k * 8, tc::sdesc_at(vd, k * 2048), IDESC_O, k > 0 ? 1u : acc0);
+          else tc::mma_f16_ts(o_dst, p_src + k * 8, tc::sdesc_at(vd, k * 2048), IDESC_O, k > 0 ? 1u : acc0);
+        }
+        if (CG == 2) {
+          tc::mma_commit_pair(&o_upd[s], (uint16_t)3);
+          tc::mma_commit_pair(&v_empty[ks], (uint16_t)3);
+        } else {
+          tc::mma_commit(&o_upd[s]);
+          tc::mma_commit(&v_empty[ks]);
+        }
         if (j + 2 < nblk && !issue_s(j + 2)) ok = false;
       }
       if (!ok) *abort_flag = 1;
@@ -300,7 +354,12 @@ __global__ void __launch_bounds__(320, 1)
       l = l * alpha + (rs2.x + rs2.y);
       tc::tmem_wait_st();
       tc::tc_fence_before();
-      tc::mbar_arrive(&p_full[g]);
+      if (CG == 2) {  // one arrival per warp on the leader's barrier, after every lane's TMEM stores
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive_cluster(leader_bar(&p_full[g]));
+      } else {
+        tc::mbar_arrive(&p_full[g]);
+      }
     }
     // ---------------- epilogue: combine the two groups, O / l -> global, lse ----------------
     // Each group's last PV completing implies every S MMA (hence every read of Q) is done, so the
@@ -351,7 +410,7 @@ __global__ void __launch_bounds__(320, 1)
               make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         tc::fence_async_shared();
         __syncwarp();
-        if (lane == 0) {
+        if (lane == 0 && q0 + quarter * 32 < p.Sq) {  // boxes wholly past Sq (ragged last tile or pair) are skipped
           tc::tma_store_4d(&tmO, buf, c * 32, (int32_t)(q0 + quarter * 32), h, b);
           tc::bulk_commit();
         }
@@ -368,10 +427,13 @@ __global__ void __launch_bounds__(320, 1)
   __syncwarp();
   tc::tc_fence_before();
   __syncthreads();
+  // pairs: neither CTA frees its TMEM or leaves while the other may still arrive on its barriers
+  if (CG == 2) tc::cluster_sync();
   if (warp == 1) {
     __syncwarp();
     tc::tc_fence_after();
-    tc::tmem_dealloc(tbase, C::TMEM_COLS);
+    if (CG == 2) tc::tmem_dealloc_pair(tbase, C::TMEM_COLS);
+    else tc::tmem_dealloc(tbase, C::TMEM_COLS);
   }
 }
 
@@ -411,19 +473,20 @@ bool attn_tc_eligible(const b2_attn_args* a) {
   return true;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int CG>
 int launch_fwd(const b2_attn_args* a, cudaStream_t st) {
-  using C = FwdCfg<D>;
+  using C = FwdCfg<D, CG>;
+  auto kern = attn_fwd_tc<D, BF16, CG>;
   static bool attr = false;
   if (!attr) {
-    if (int rc = check_cuda(cudaFuncSetAttribute(attn_fwd_tc<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
+    if (int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
                             "attn_fwd_tc attr"))
       return rc;
     attr = true;
   }
   CUtensorMap tq, tk, tv, to;
   if (!make_bhsd_map(&tq, a->q, a->q_s, a->B, a->H, a->Sq, D, BF16, 128) ||
-      !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, D, BF16, 128) ||
+      !make_bhsd_map(&tk, a->k, a->k_s, a->B, a->H, a->Sk, D, BF16, C::KROWS) ||
       !make_bhsd_map(&tv, a->v, a->v_s, a->B, a->H, a->Sk, D, BF16, 128) ||
       !make_bhsd_map(&to, a->o, a->o_s, a->B, a->H, a->Sq, D, BF16, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(B2_ERR_ARG, "attn_tc: tensor map rejected");
@@ -435,14 +498,53 @@ int launch_fwd(const b2_attn_args* a, cudaStream_t st) {
   for (int i = 0; i < 3; ++i) p.o_s[i] = a->o_s[i];
   p.lse = a->lse;
   p.err = device_error_ptr();
-  dim3 grid((unsigned)((a->Sq + 127) / 128), (unsigned)(a->B * a->H));
-  return launch_pdl("attn_fwd_tc", attn_fwd_tc<D, BF16>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, to, p);
+  if (CG == 1) {
+    dim3 grid((unsigned)((a->Sq + 127) / 128), (unsigned)(a->B * a->H));
+    return launch_pdl("attn_fwd_tc", kern, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, to, p);
+  }
+  // CTA pairs: clusters of two along x, each pair over 256 query rows; programmatic dependent launch
+  // as for single CTAs (outside stream capture)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(((a->Sq + 255) / 256) * 2), (unsigned)(a->B * a->H));
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cs = cudaStreamCaptureStatusActive;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = (pdl_enabled() && cs == cudaStreamCaptureStatusNone) ? 2 : 1;
+  cudaError_t e;
+  {
+    LaunchScope ls("attn_fwd_tc_pair", st);
+    e = cudaLaunchKernelEx(&cfg, kern, tq, tk, tv, to, p);
+  }
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail_cuda(e, "attn_fwd_tc_pair");
+  }
+  return after_launch("attn_fwd_tc_pair");
 }
 
 int attn_tc_fwd(const b2_attn_args* a, cudaStream_t st) {
   const bool bf16 = a->dtype == B2_BF16;
-  if (a->D == 128) return bf16 ? launch_fwd<128, true>(a, st) : launch_fwd<128, false>(a, st);
-  return bf16 ? launch_fwd<64, true>(a, st) : launch_fwd<64, false>(a, st);
+  // CTA pairs need D = 128 (V splits into two 64-column halves) and at least two query tiles. They are
+  // opt-in (B2_ATTN_FWD_PAIRS=1): measured at B1 H16 S1024 D128 the pair form takes 21.3 us per forward
+  // against 19.9 us for single CTAs (the softmax hand-off, not operand bandwidth, bounds this kernel)
+  static const bool pairs_on = [] {
+    const char* e = getenv("B2_ATTN_FWD_PAIRS");
+    return e && e[0] == '1';
+  }();
+  if (a->D == 128 && a->Sq > 128 && pairs_on) return bf16 ? launch_fwd<128, true, 2>(a, st) : launch_fwd<128, false, 2>(a, st);
+  if (a->D == 128) return bf16 ? launch_fwd<128, true, 1>(a, st) : launch_fwd<128, false, 1>(a, st);
+  return bf16 ? launch_fwd<64, true, 1>(a, st) : launch_fwd<64, false, 1>(a, st);
 }
 
 int attn_simt_bwd_dispatch(const b2_attn_args* a, cudaStream_t st);  // attn_simt.cu

@@ -102,6 +102,12 @@ struct TcParams {
   int epi;
   void* aux;
   int64_t aux_ld;
+  // int8 LoRA side path: one extra 64-wide K block after the k_blocks of the weight, whose A tile is
+  // the [M, r] activation-side operand (tensor map tmH) and whose B tile the dequant warps copy from
+  // lora_b ([N, r] forward, [r, K] transposed); k_total = k_blocks + (lora_r > 0)
+  const void* lora_b;
+  int64_t lora_b_ld;
+  int lora_r, k_total;
 };
 
 enum : int { EPI_NONE = 0, EPI_GELU = 1, EPI_GELU_BWD = 2 };
@@ -199,7 +205,7 @@ __device__ __forceinline__ void dequant16(const int4& raw, float s, uint32_t* w)
 template <int BN, bool BF16, int DEQ, int MSUB, int CG>
 __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, TcParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH, TcParams p) {
   using C = Cfg<BN, DEQ, MSUB, CG>;
   constexpr int BNC = C::BNC;
   constexpr int S = C::STAGES;
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
 
   auto k_range = [&](int t, int& kb0, int& kb1) {
     kb0 = (t / total_tiles) * p.kps;
-    kb1 = kb0 + p.kps < p.k_blocks ? kb0 + p.kps : p.k_blocks;
+    kb1 = kb0 + p.kps < p.k_total ? kb0 + p.kps : p.k_total;
   };
   auto tile_coords = [&](int t, int& m0, int& n0, int& b) {
     t %= total_tiles;
@@ -289,6 +295,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     if (lane == 0) {
       tc::tma_prefetch_desc(&tmA);
       tc::tma_prefetch_desc(&tmB);
+      if (p.lora_r) tc::tma_prefetch_desc(&tmH);
       if (p.c_tma) tc::tma_prefetch_desc(&tmC);
       int stage = 0;
       uint32_t phase = 0;
@@ -312,7 +319,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
             // this CTA's BMT rows of A land in its own shared memory and count on the leader's full
             // barrier, which the leader arms for both CTAs' bytes
             if (rank == 0) tc::mbar_arrive_expect_tx(&full[stage], (uint32_t)(C::STAGE * CG));
-            tc::tma_load_2d_pair(sa, &tmA, full0 + 8u * (uint32_t)stage, k0, m0 + (int)rank * C::BMT);
+            if (kb < p.k_blocks) tc::tma_load_2d_pair(sa, &tmA, full0 + 8u * (uint32_t)stage, k0, m0 + (int)rank * C::BMT);
+            else tc::tma_load_2d_pair(sa, &tmH, full0 + 8u * (uint32_t)stage, 0, m0 + (int)rank * C::BMT);
             issued[stage] += 1;
             if (++stage == S) {
               stage = 0;
@@ -322,7 +330,9 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
           }
           const uint32_t bytes = C::STAGE;
           tc::mbar_arrive_expect_tx(&full[stage], bytes);
-          if (!p.a_mn) {  // one box of BMT rows x 64 k
+          if (kb >= p.k_blocks) {  // the LoRA block: A = the [M, r] side-path operand (K-major)
+            tc::tma_load_2d(sa, &tmH, &full[stage], 0, m0);
+          } else if (!p.a_mn) {  // one box of BMT rows x 64 k
             if (p.a3d) tc::tma_load_3d(sa, &tmA, &full[stage], k0, m0, b);
             else tc::tma_load_2d(sa, &tmA, &full[stage], k0, m0);
           } else {  // BMT/64 boxes of 64 m x 64 k
@@ -680,7 +690,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
         tile_coords(t, m0, n0, b);
         k_range(t, kb0, kb1);
         n0 += (int)rank * BNC;  // pairs: this CTA stages B rows [n0 + rank * BN/2, + BN/2)
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1 && kb < p.k_blocks; ++kb) {  // (the LoRA block has no int8 tile)
           if (!tc::mbar_wait(&rempty[rs], rph ^ 1, p.err) || *abort_flag) {
             ok = false;
             *abort_flag = 1;
@@ -706,7 +716,8 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     // ------------------------------- int8 dequant -------------------------------------------
     const int dw = warp - 6 - (warp > 9 ? 1 : 0) - (warp > 13 ? 1 : 0);  // 0 .. 7
     const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
-    int gk = 0;  // K blocks dequantised so far (B ring position)
+    int gk = 0;  // K blocks staged so far (B ring position)
+    int gr = 0;  // int8 tiles converted so far (raw ring position; the LoRA block has none)
     constexpr int FIPT = (BNC * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
     float fsc[FIPT];
     constexpr int IPT = (64 * (BNC / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // transposed items per thread
@@ -721,7 +732,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
       for (int kb = kb0; kb < kb1; ++kb) {
         // forward scales, loaded before the waits so that their latency overlaps them: block-64
         // scales change with the K block, per-row scales are loaded once per tile
-        if (!p.b_mn && (p.scale_layout == 0 || kb == kb0)) {
+        if (!p.b_mn && kb < p.k_blocks && (p.scale_layout == 0 || kb == kb0)) {
 #pragma unroll
           for (int u = 0; u < FIPT; ++u) {  // every scale load in flight before the first is used
             const int i = dt + u * NDQ;
@@ -733,8 +744,9 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
                            : reinterpret_cast<const float*>(p.scale)[gn];
           }
         }
-        const int rs = gk % NR;
-        if (p.b_mn) {
+        const int rs = gr % NR;
+        const bool lora_blk = kb >= p.k_blocks;
+        if (p.b_mn && !lora_blk) {
           // transposed form: the scale of reduction row nf = kb * 64 + i, loaded before the waits
 #pragma unroll
           for (int u = 0; u < IPT; ++u) {  // every scale load in flight before the first is used
@@ -749,7 +761,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
                           : reinterpret_cast<const float*>(p.scale)[nf];
           }
         }
-        if (!tc::mbar_wait(&rfull[rs], (uint32_t)((gk / NR) & 1), p.err) || *abort_flag) {
+        if (!lora_blk && (!tc::mbar_wait(&rfull[rs], (uint32_t)((gr / NR) & 1), p.err) || *abort_flag)) {
           ok = false;
           break;
         }
@@ -760,7 +772,30 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
         }
         uint8_t* sb = smem + C::OFF_B + bb * C::B_BYTES;
         const uint8_t* sr = smem + C::OFF_R + rs * C::R_BYTES;
-        if (!p.b_mn) {
+        if (lora_blk) {
+          // the LoRA block: the bf16 side-path weight copied (rows beyond r as zeros) into the same
+          // swizzled layout the dequantised tiles use; forward: lora_b [N, r], row n of the B tile is
+          // lora_b row n0 + n; transposed: lora_b [r, K], reduction row i of the tile is lora_b row i
+          const __nv_bfloat16* lb = reinterpret_cast<const __nv_bfloat16*>(p.lora_b);
+          if (!p.b_mn) {
+            for (int e = dt; e < BNC * 8; e += NDQ) {
+              const int n = e >> 3, c = e & 7;  // 16 B chunk c = k 8c..8c+7 of row n
+              const int64_t gn = (int64_t)n0 + n;
+              uint4 v = make_uint4(0u, 0u, 0u, 0u);
+              if (c * 8 < p.lora_r && gn < p.N) v = *reinterpret_cast<const uint4*>(lb + gn * p.lora_b_ld + c * 8);
+              *reinterpret_cast<uint4*>(sb + n * 128 + ((c ^ (n & 7)) << 4)) = v;
+            }
+          } else {
+            for (int e = dt; e < 64 * (BNC / 8); e += NDQ) {
+              const int i = e / (BNC / 8), g8 = e % (BNC / 8);  // reduction row i, output columns 8*g8..
+              const int64_t col = (int64_t)n0 + g8 * 8;
+              uint4 v = make_uint4(0u, 0u, 0u, 0u);
+              if (i < p.lora_r && col < p.N) v = *reinterpret_cast<const uint4*>(lb + (int64_t)i * p.lora_b_ld + col);
+              const int chunk = (g8 * 8) >> 6, g0 = ((g8 * 8) & 63) >> 3;
+              *reinterpret_cast<uint4*>(sb + chunk * 8192 + i * 128 + ((g0 ^ (i & 7)) << 4)) = v;
+            }
+          }
+        } else if (!p.b_mn) {
           // forward: raw [BNC rows n][64 bytes k]; B stage K-major SW128: row n at n*128 B,
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
 #pragma unroll
@@ -800,11 +835,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
         tc::fence_async_shared();
         __syncwarp();
         if (lane == 0) {
-          tc::mbar_arrive(&rempty[rs]);
+          if (!lora_blk) tc::mbar_arrive(&rempty[rs]);
           if (CG == 2) tc::mbar_arrive_cluster(bready0 + 8u * (uint32_t)bb);
           else tc::mbar_arrive(&bready[bb]);
         }
         ++gk;
+        if (!lora_blk) ++gr;
       }
     }
     if (ok && CG == 2 && dw == 0 && lane == 0) {
@@ -838,7 +874,12 @@ bool tma_ok_stride(int64_t s_elems, int esz) { return ((s_elems * esz) % 16) == 
 
 template <int BN, bool BF16, int DEQ, int MSUB, int CG = 1>
 int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc_, const TcParams& p, cudaStream_t st,
-                  const char* name) {
+                  const char* name, const CUtensorMap* th = nullptr) {
+  CUtensorMap th0;  // the LoRA operand's map (unused without a side path)
+  if (!th) {
+    memset(&th0, 0, sizeof(th0));
+    th = &th0;
+  }
   using C = Cfg<BN, DEQ, MSUB, CG>;
   auto kern = gemm_tc_kernel<BN, BF16, DEQ, MSUB, CG>;
   static int max_pairs = 0;  // set once per process (single device per process)
@@ -880,7 +921,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     cudaError_t e;
     {
       LaunchScope ls(name, st);
-      e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_, p);
+      e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_, *th, p);
     }
     if (e != cudaSuccess) {
       (void)cudaGetLastError();
@@ -890,7 +931,7 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
   }
   int grid = std::min(tiles, device_info().sm_count);
   LaunchScope ls(name, st);
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, tc_, p);
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, tc_, *th, p);
   return after_launch(name);
 }
 
@@ -1041,6 +1082,7 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
   p.m_tiles = (int)((a->M + BMT - 1) / BMT);
   p.n_tiles = (int)((a->N + BN - 1) / BN);
   p.k_blocks = (int)((a->K + BK - 1) / BK);
+  p.k_total = p.k_blocks;
   p.a_mn = !(a->a_sk == 1 && (a->M == 1 || tma_ok_stride(a->a_sm, 2)));
   p.b_mn = !(a->b_sk == 1 && (a->N == 1 || tma_ok_stride(a->b_sn, 2)));
   p.a3d = a->batch > 1 && a->a_sb != 0;
@@ -1182,7 +1224,7 @@ Int8Plan int8_plan(const b2_int8_gemm_args* a) {
   }
   if (best.bn == 0) best = Int8Plan{128, 2, 1, k_blocks, 1};
   // split-K over 256x256 tiles (CTA pairs: 512x256) when too few tiles fill the GPU and K is long
-  if (!forced && !a->epilogue && a->workspace_bytes > 0 && k_blocks >= 64) {
+  if (!forced && !a->epilogue && !a->lora_r && a->workspace_bytes > 0 && k_blocks >= 64) {
     for (int cg = 1; cg <= 2; ++cg) {
       if (forced_cg && cg != forced_cg) continue;
       const int64_t rows = 256 * cg, cap = sms / cg;
@@ -1227,6 +1269,11 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
     return fail(B2_ERR_ARG, "int8_gemm: epilogue 1 (GELU) needs the forward form, 2 (GELU backward) the transposed form");
   if (a->epilogue && (!a->aux || ((uintptr_t)a->aux & 15) || a->aux_ld < out_cols || a->aux_ld % 8))
     return fail(B2_ERR_ARG, "int8_gemm: the GELU epilogue needs a 16-byte aligned bf16 aux with aux_ld >= out_cols, a multiple of 8");
+  if (a->lora_r && (a->lora_r < 8 || a->lora_r > 64 || a->lora_r % 8 || !a->lora_h || !a->lora_b ||
+                    ((uintptr_t)a->lora_h & 15) || ((uintptr_t)a->lora_b & 15) || a->lora_h_ld < a->lora_r ||
+                    a->lora_h_ld % 8 || a->lora_b_ld % 8 || a->lora_b_ld < (a->transpose_w ? a->K : a->lora_r)))
+    return fail(B2_ERR_ARG, "int8_gemm: LoRA operands need 8 <= r <= 64 (a multiple of 8), 16-byte aligned bf16 rows and "
+                            "leading dims that are multiples of 8");
   cudaStream_t st = (cudaStream_t)stream;
   if (a->workspace && ((uintptr_t)a->workspace & 15)) return fail(B2_ERR_ARG, "int8_gemm: workspace must be 16-byte aligned");
   b2_int8_gemm_args aa = *a;
@@ -1247,6 +1294,18 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   p.scale = a->scale, p.scale_layout = a->scale_layout, p.scale_nb = (a->K + 63) / 64, p.deq_rows = a->N;
   p.ksplit = best.ksplit, p.kps = best.kps;
   if (p.ksplit > 1) p.partial = (float*)a->workspace;
+  // the LoRA side path: one more K block (the plan never splits K when there is one)
+  p.lora_r = a->lora_r, p.lora_b = a->lora_b, p.lora_b_ld = a->lora_b_ld;
+  p.k_total = p.k_blocks + (a->lora_r ? 1 : 0);
+  if (a->lora_r) p.kps = p.k_total;
+  CUtensorMap th;
+  memset(&th, 0, sizeof(th));
+  if (a->lora_r) {  // [M, r] bf16, read as 64-wide boxes (columns past r are filled with zeros)
+    uint64_t dims[2] = {(uint64_t)a->lora_r, (uint64_t)a->M}, strides[1] = {(uint64_t)a->lora_h_ld * 2};
+    uint32_t box[2] = {64, (uint32_t)BMT};
+    if (!make_tmap(&th, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a->lora_h, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(B2_ERR_ARG, "int8_gemm: tensor map for the LoRA operand rejected");
+  }
   CUtensorMap tcm;
   memset(&tcm, 0, sizeof(tcm));
   setup_cmap(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, p);
@@ -1272,16 +1331,16 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
   int rc;
   if (best.cg == 2) {
     const char* pname = a->transpose_w ? "int8_gemm_dx_pair" : "int8_gemm_fwd_pair";
-    if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2, 2>(ta, tb, tcm, p, st, pname);
-    else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2, 2>(ta, tb, tcm, p, st, pname);
-    else if (best.msub == 2) rc = launch_kernel<128, true, 2, 2, 2>(ta, tb, tcm, p, st, pname);
-    else rc = launch_kernel<256, true, 2, 1, 2>(ta, tb, tcm, p, st, pname);
-  } else if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name);
-  else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name);
-  else if (best.msub == 2 && BN == 128) rc = launch_kernel<128, true, 2, 2>(ta, tb, tcm, p, st, name);
-  else if (best.msub == 2 && BN == 96) rc = launch_kernel<96, true, 2, 2>(ta, tb, tcm, p, st, name);
-  else if (BN == 256) rc = launch_kernel<256, true, 2, 1>(ta, tb, tcm, p, st, name);
-  else rc = launch_kernel<128, true, 2, 1>(ta, tb, tcm, p, st, name);
+    if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2, 2>(ta, tb, tcm, p, st, pname, &th);
+    else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2, 2>(ta, tb, tcm, p, st, pname, &th);
+    else if (best.msub == 2) rc = launch_kernel<128, true, 2, 2, 2>(ta, tb, tcm, p, st, pname, &th);
+    else rc = launch_kernel<256, true, 2, 1, 2>(ta, tb, tcm, p, st, pname, &th);
+  } else if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name, &th);
+  else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name, &th);
+  else if (best.msub == 2 && BN == 128) rc = launch_kernel<128, true, 2, 2>(ta, tb, tcm, p, st, name, &th);
+  else if (best.msub == 2 && BN == 96) rc = launch_kernel<96, true, 2, 2>(ta, tb, tcm, p, st, name, &th);
+  else if (BN == 256) rc = launch_kernel<256, true, 2, 1>(ta, tb, tcm, p, st, name, &th);
+  else rc = launch_kernel<128, true, 2, 1>(ta, tb, tcm, p, st, name, &th);
   if (rc || p.ksplit == 1) return rc;
   const int64_t total = a->M * out_cols;
   const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)device_info().sm_count * 8);

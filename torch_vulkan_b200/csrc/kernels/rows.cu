@@ -735,7 +735,9 @@ LnPlan ln_plan(const b2_layernorm_args* a, bool fwd) {
     int64_t blocks = (a->rows + rpb - 1) / rpb;
     // forward: enough blocks to fill the GPU. backward: two blocks per SM walking several rows with
     // the next row prefetched, which keeps the weight-gradient partial slots (and their reduction) few
-    int64_t cap = fwd ? (int64_t)sms * 4 : (p.group == 32 ? (int64_t)sms / 2 : (int64_t)sms * 2);
+    // (forward with a 256-thread group per row: up to eight rows per SM at once, so a [1024, 2048] input is
+    // read in a single wave of loads)
+    int64_t cap = fwd ? (int64_t)sms * (p.group == 256 ? 8 : 4) : (p.group == 32 ? (int64_t)sms / 2 : (int64_t)sms * 2);
     p.grid = (int)std::max<int64_t>(1, std::min(blocks, cap));
     p.nslots = (int64_t)p.grid * rpb;
   } else {

@@ -630,8 +630,26 @@ at::Tensor int8_workspace(b2_int8_gemm_args& g, const at::Tensor& like) {
 
 // y[..., N] = x[..., K] @ (q * scale)^T + bias; with `gelu_out` the GEMM's epilogue also writes
 // gelu_tanh(y) there (the DiT MLP's fc1: y is the pre-activation the backward needs)
+// LoRA side operands of one int8 GEMM: h [rows, r] and the weight-side matrix, both bf16; returns r.
+int64_t lora_operands(b2_int8_gemm_args& g, const at::Tensor* h, const at::Tensor* w, at::Tensor& hc, at::Tensor& wc,
+                      int64_t rows, bool transposed) {
+  if (!h) return 0;
+  TORCH_CHECK(h->scalar_type() == at::kBFloat16 && w->scalar_type() == at::kBFloat16, "int8 LoRA: bf16 operands required");
+  hc = h->reshape({-1, h->size(-1)});
+  if (!hc.is_contiguous()) hc = hc.contiguous();
+  wc = w->contiguous();
+  const int64_t r = hc.size(1);
+  TORCH_CHECK(hc.size(0) == rows && r >= 8 && r <= 64 && r % 8 == 0, "int8 LoRA: h must be [rows, r] with 8 <= r <= 64, r % 8 == 0");
+  TORCH_CHECK(transposed ? (wc.dim() == 2 && wc.size(0) == r) : (wc.dim() == 2 && wc.size(1) == r),
+              "int8 LoRA: the weight-side operand must be [N, r] (forward) or [r, K] (dX)");
+  g.lora_h = hc.data_ptr(), g.lora_b = wc.data_ptr();
+  g.lora_h_ld = r, g.lora_b_ld = wc.size(1), g.lora_r = (int32_t)r;
+  return r;
+}
+
 at::Tensor int8_fwd_impl(const at::Tensor& x0, const at::Tensor& q, const at::Tensor& scale0,
-                         const std::optional<at::Tensor>& bias0, at::Tensor* gelu_out) {
+                         const std::optional<at::Tensor>& bias0, at::Tensor* gelu_out,
+                         const at::Tensor* lora_h = nullptr, const at::Tensor* lora_b = nullptr) {
   TORCH_CHECK(x0.is_cuda() && q.is_cuda(), "int8_linear: CUDA tensors required");
   TORCH_CHECK(x0.scalar_type() == at::kBFloat16, "int8_linear: x must be bfloat16");
   TORCH_CHECK(q.scalar_type() == at::kChar && q.dim() == 2 && q.is_contiguous(), "int8_linear: q must be contiguous int8 [N,K]");
@@ -663,6 +681,9 @@ at::Tensor int8_fwd_impl(const at::Tensor& x0, const at::Tensor& q, const at::Te
   g.scale_layout = layout;
   g.transpose_w = 0;
   if (gelu_out) g.epilogue = 1, g.aux = gelu_out->data_ptr(), g.aux_ld = N;
+  at::Tensor lh, lb;
+  if (lora_h) TORCH_CHECK(lora_b->size(0) == N, "int8_lora_fwd: b must be [N, r]");
+  lora_operands(g, lora_h, lora_b, lh, lb, g.M, false);
   at::Tensor ws = int8_workspace(g, x);
   b2_check(b2_int8_gemm(&g, cur_stream()), gelu_out ? "int8_linear_gelu_fwd" : "int8_linear_fwd");
   count(gelu_out ? "b2::int8_linear_gelu" : "b2::int8_linear");
@@ -686,7 +707,8 @@ std::tuple<at::Tensor, at::Tensor> b2_int8_linear_gelu_fwd(const at::Tensor& x0,
 
 // dx[..., K] = dy[..., N] @ (q * scale); with `h` (the pre-activation of a GELU that follows this
 // linear's input) the epilogue returns dx * gelu_tanh'(h) instead
-at::Tensor int8_dx_impl(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0, const at::Tensor* h) {
+at::Tensor int8_dx_impl(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0, const at::Tensor* h,
+                        const at::Tensor* lora_h = nullptr, const at::Tensor* lora_a = nullptr) {
   TORCH_CHECK(dy0.is_cuda() && q.is_cuda() && dy0.scalar_type() == at::kBFloat16, "int8_linear_dx: bf16 CUDA dy required");
   c10::cuda::CUDAGuard guard(dy0.device());
   const int64_t N = q.size(0), K = q.size(1);
@@ -712,6 +734,9 @@ at::Tensor int8_dx_impl(const at::Tensor& dy0, const at::Tensor& q, const at::Te
   g.scale_layout = layout;
   g.transpose_w = 1;
   if (h) g.epilogue = 2, g.aux = hh.data_ptr(), g.aux_ld = K;
+  at::Tensor lh, la;
+  if (lora_h) TORCH_CHECK(lora_a->dim() == 2 && lora_a->size(1) == K, "int8_lora_dx: a must be [r, K]");
+  lora_operands(g, lora_h, lora_a, lh, la, g.M, true);
   at::Tensor ws = int8_workspace(g, dy);
   b2_check(b2_int8_gemm(&g, cur_stream()), h ? "int8_linear_dx_gelu" : "int8_linear_dx");
   count(h ? "b2::int8_linear_dx_gelu" : "b2::int8_linear_dx");
@@ -725,6 +750,23 @@ at::Tensor b2_int8_linear_dx(const at::Tensor& dy0, const at::Tensor& q, const a
 at::Tensor b2_int8_linear_dx_gelu(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0,
                                   const at::Tensor& h) {
   return int8_dx_impl(dy0, q, scale0, &h);
+}
+
+// y = x @ (q * scale)^T + bias + h @ b^T: the LoRA up-projection (b = B * alpha / r, h = x @ A^T) added by
+// the int8 GEMM itself as one more reduction block
+at::Tensor b2_int8_lora_fwd(const at::Tensor& x0, const at::Tensor& q, const at::Tensor& scale0,
+                            const std::optional<at::Tensor>& bias0, const at::Tensor& h, const at::Tensor& b) {
+  at::Tensor y = int8_fwd_impl(x0, q, scale0, bias0, nullptr, &h, &b);
+  count("b2::int8_lora_fwd");
+  return y;
+}
+
+// dx = dy @ (q * scale) + dh @ a: the LoRA input gradient (dh = dy @ B * alpha / r, a = A) in the same GEMM
+at::Tensor b2_int8_lora_dx(const at::Tensor& dy0, const at::Tensor& q, const at::Tensor& scale0, const at::Tensor& dh,
+                           const at::Tensor& a) {
+  at::Tensor dx = int8_dx_impl(dy0, q, scale0, nullptr, &dh, &a);
+  count("b2::int8_lora_dx");
+  return dx;
 }
 
 // One AdamW step for a list of parameters (the arithmetic and roundings of torch.optim.AdamW with
@@ -833,6 +875,8 @@ TORCH_LIBRARY(b2, m) {
   m.def("int8_linear_dx(Tensor dy, Tensor q, Tensor scale) -> Tensor");
   m.def("int8_linear_gelu_fwd(Tensor x, Tensor q, Tensor scale, Tensor? bias) -> (Tensor, Tensor)");
   m.def("int8_linear_dx_gelu(Tensor dy, Tensor q, Tensor scale, Tensor h) -> Tensor");
+  m.def("int8_lora_fwd(Tensor x, Tensor q, Tensor scale, Tensor? bias, Tensor h, Tensor b) -> Tensor");
+  m.def("int8_lora_dx(Tensor dy, Tensor q, Tensor scale, Tensor dh, Tensor a) -> Tensor");
   m.def("adamw_step_(Tensor(a!)[] params, Tensor[] grads, Tensor(b!)[] exp_avgs, Tensor(c!)[] exp_avg_sqs, float lr, "
         "float beta1, float beta2, float eps, float weight_decay, int step) -> ()");
   m.def("set_enabled(bool on) -> ()", &op_set_enabled);
@@ -849,5 +893,7 @@ TORCH_LIBRARY_IMPL(b2, CUDA, m) {
   m.impl("int8_linear_dx", &b2_int8_linear_dx);
   m.impl("int8_linear_gelu_fwd", &b2_int8_linear_gelu_fwd);
   m.impl("int8_linear_dx_gelu", &b2_int8_linear_dx_gelu);
+  m.impl("int8_lora_fwd", &b2_int8_lora_fwd);
+  m.impl("int8_lora_dx", &b2_int8_lora_dx);
   m.impl("adamw_step_", &b2_adamw_step_op);
 }

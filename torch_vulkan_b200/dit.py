@@ -54,25 +54,23 @@ class LoRAInt8Linear(nn.Module):
         self.scale = alpha / rank
 
     def forward(self, x):
-        y = self.base(x)
-        h = F.linear(x, self.lora_down)
-        # the up-projection accumulates onto the base output in one GEMM: y + (h B^T) * alpha / r
-        out = torch.addmm(y.reshape(-1, y.shape[-1]), h.reshape(-1, h.shape[-1]), self.lora_up.t(), alpha=self.scale)
-        return out.view(y.shape)
+        # the up-projection (h B^T) * alpha / r is one more reduction block of the int8 GEMM
+        b = self.lora_up if self.scale == 1.0 else self.lora_up * self.scale
+        return tv.int8_lora_linear(x, self.base.q, self.base.scale, self.base.bias, self.lora_down, b)
 
 
 def stacked_lora_forward(x, q, scale, bias, mods):
     """LoRAInt8Linear.forward of several modules that read the same input x, with their frozen int8
-    bases stacked in (q, scale, bias): one int8 GEMM, one down-projection GEMM over the stacked A_i and
-    one up-projection GEMM over the block-diagonal B_i accumulated onto the base output (backward: one
-    dX GEMM, and one GEMM each for dh, dA and dB, instead of one of each per module). Returns one
-    [..., out_i] view per module."""
-    y = tv.int8_linear(x, q, scale, bias)
-    h = F.linear(x, torch.cat([m.lora_down for m in mods], 0))
-    bd = torch.block_diag(*[m.lora_up for m in mods])
-    n = y.shape[-1]
-    out = torch.addmm(y.reshape(-1, n), h.reshape(-1, h.shape[-1]), bd.t(), alpha=mods[0].scale)
-    return out.view(y.shape).split([m.base.q.shape[0] for m in mods], dim=-1)
+    bases stacked in (q, scale, bias): one down-projection GEMM over the stacked A_i, then one int8 GEMM
+    whose last reduction block adds the up-projection over the block-diagonal B_i (backward: one dX GEMM
+    that also adds dh @ A, and one GEMM each for dh, dA and dB, instead of one of each per module).
+    Returns one [..., out_i] view per module."""
+    a = torch.cat([m.lora_down for m in mods], 0)
+    b = torch.block_diag(*[m.lora_up for m in mods])
+    if mods[0].scale != 1.0:
+        b = b * mods[0].scale
+    out = tv.int8_lora_linear(x, q, scale, bias, a, b)
+    return out.split([m.base.q.shape[0] for m in mods], dim=-1)
 
 
 class DiTBlock(nn.Module):
@@ -227,7 +225,10 @@ class LoRATrainer:
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         self.reducer.zero_grad()  # re-arm the hooks so the captured backward launches every bucket
-        with torch.cuda.graph(graph):
+        # with NCCL, the process group's watchdog thread queries events while this thread captures; the
+        # thread-local capture mode keeps those queries from invalidating the capture
+        mode = "thread_local" if self.reducer.world > 1 else "global"
+        with torch.cuda.graph(graph, capture_error_mode=mode):
             for flat in self.reducer.flats:  # gradients accumulate into the bucket buffers
                 flat.zero_()
             loss = F.mse_loss(self.model(x, text, cond).float(), target.float())
