@@ -687,14 +687,20 @@ def run_case(name, iters):
             a, b = (torch.randn(8192, 8192, generator=g).to(torch.bfloat16).to(dev) for _ in range(2))
             fn = lambda: torch.mm(a, b)  # noqa: E731
         else:
+            # the LoRA projections of the stacked q/k/v group (rank 48) and the dense MLP shapes at 4096
+            # tokens (4096 x 8192 x 2048 and 4096 x 2048 x 8192, the fc1 / fc2 forms of a bf16 linear)
             x = torch.randn(4096, 2048, generator=g).to(torch.bfloat16).to(dev)
             w_down = torch.randn(48, 2048, generator=g).to(torch.bfloat16).to(dev)
             w_up = torch.randn(6144, 48, generator=g).to(torch.bfloat16).to(dev)
             y = torch.randn(4096, 6144, generator=g).to(torch.bfloat16).to(dev)
+            w1 = torch.randn(8192, 2048, generator=g).to(torch.bfloat16).to(dev)
+            w2 = torch.randn(2048, 8192, generator=g).to(torch.bfloat16).to(dev)
 
             def fn():
                 h = torch.nn.functional.linear(x, w_down)
                 torch.addmm(y, h, w_up.t())
+                a1 = torch.nn.functional.linear(x, w1)
+                torch.nn.functional.linear(a1, w2)
     elif name == "int8":
         x = torch.randn(1024, 2048, generator=g).to(torch.bfloat16).to(dev)
         qw = torch.randint(-127, 128, (6144, 2048), generator=g, dtype=torch.int8).to(dev)

@@ -186,3 +186,51 @@ def test_pair_forward_opt_in_matches_oracle():
     assert "attn_fwd_tc_pair" in res["kernels"], res["kernels"]
     for B, H, Sq, Sk, dt, e, le in res["cases"]:
         assert e < 2e-2 and le <= 1e-3, (B, H, Sq, Sk, dt, e, le)
+
+
+BWD_CHILD = r"""
+import json, sys
+sys.path.insert(0, ROOT)
+import torch
+import torch.nn.functional as F
+import oracle
+import torch_vulkan_b200 as tv
+
+tv.set_fused_attention("on")
+tv.profile_enable(True)
+g = torch.Generator().manual_seed(12)
+out = []
+for B, H, Sq, Sk in [(1, 2, 200, 77), (2, 3, 65, 300), (1, 1, 1, 129), (1, 16, 1024, 1024), (2, 2, 333, 512)]:
+    q, k, v, do = (torch.randn(B, H, S, 128, generator=g).to(torch.bfloat16) for S in (Sq, Sk, Sk, Sq))
+    qd, kd, vd = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    F.scaled_dot_product_attention(qd, kd, vd).backward(do.cuda())
+    refs = oracle.sdpa_bwd(q, k, v, do)
+    errs = [((x.grad.cpu().double() - r).norm() / r.norm()).item() for x, r in zip((qd, kd, vd), refs)]
+    out.append([B, H, Sq, Sk] + errs)
+torch.cuda.synchronize()
+kernels = [ln.split("\t")[0] for ln in tv.profile().splitlines() if ln]
+print("RESULT " + json.dumps({"cases": out, "kernels": kernels, "validation_errors": tv.validation_errors()}))
+"""
+
+
+@pytest.mark.parametrize("dsout", ["1", "0"])
+def test_tc_backward_forms_ragged(dsout):
+    """Both forms of the tcgen05 backward at ragged D = 128 shapes (query and key counts off the 64 / 128
+    tiles, B > 1), each pinned by B2_ATTN_BWD_DSOUT and compared with float64: dS^T stored to L2 and one dQ
+    GEMM after the kernel (=1; by default taken when the key-tile CTAs fill at most half the GPU), and the
+    in-kernel dQ^T with fp32 reductions into an L2 accumulator (=0)."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", BWD_CHILD.replace("ROOT", repr(root))], capture_output=True,
+                       text=True, timeout=600, cwd=root, env=dict(os.environ, B2_ATTN_BWD_DSOUT=dsout))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("RESULT ")][-1][len("RESULT "):])
+    assert res["validation_errors"] == 0
+    assert "attn_bwd_tc" in res["kernels"], res["kernels"]
+    assert ("attn_dq_convert" in res["kernels"]) == (dsout == "0"), res["kernels"]
+    for B, H, Sq, Sk, eq, ek, ev in res["cases"]:
+        assert max(eq, ek, ev) < 2e-2, (dsout, B, H, Sq, Sk, eq, ek, ev)

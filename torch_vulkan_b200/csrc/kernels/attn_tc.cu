@@ -584,6 +584,10 @@ struct BwdCfg {
                             TMEM_COLS = 512;
 };
 
+// DSOUT = false: dQ^T_i = K^T dS^T_i is a fifth MMA per tile, added into an fp32 accumulator in L2.
+// DSOUT = true (dS fits in L2): the dS^T tile in shared memory is stored by TMA to a bf16 [bh][Sk][sq_pad]
+// buffer (tmDQ then maps that buffer) and one tensor-core GEMM dQ = scale * dS K follows the kernel.
+template <bool DSOUT>
 __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -739,14 +743,16 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
           tc::mma_f16_ts(tbase + C::T_DK, tbase + C::T_DST + k * 8, tc::sdesc_at(qmd, k * 2048), IDESC_KV, k > 0 ? 1u : acc0);
         tc::mma_commit(&q_empty[qs]);
         tc::mma_commit(ptm_empty);
-        // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
-        if (i > 0 && !tc::mbar_wait(dq_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
-        tc::tc_fence_after();
+        if constexpr (!DSOUT) {
+          // dQ^T = K^T dS^T (M = D, N = 64 queries, K = 128 keys) once the previous dQ^T was drained
+          if (i > 0 && !tc::mbar_wait(dq_empty, (uint32_t)((i - 1) & 1), p.err)) { ok = false; break; }
+          tc::tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < C::BKV / 16; ++k)
-          tc::mma_f16_ss(tbase + C::T_DQ, tc::sdesc_at(ktd, k * 2048), tc::sdesc_at(dsd, k * 2048), IDESC_DQ, k > 0 ? 1u : 0u);
-        tc::mma_commit(dq_full);
-        tc::mma_commit(&pds_empty[s]);
+          for (int k = 0; k < C::BKV / 16; ++k)
+            tc::mma_f16_ss(tbase + C::T_DQ, tc::sdesc_at(ktd, k * 2048), tc::sdesc_at(dsd, k * 2048), IDESC_DQ, k > 0 ? 1u : 0u);
+          tc::mma_commit(dq_full);
+          tc::mma_commit(&pds_empty[s]);
+        }
       }
       if (ok) tc::mma_commit(dkv_full);
       else *abort_flag = 1;
@@ -850,10 +856,27 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
       tc::tmem_wait_st();
       tc::fence_async_shared();
       tc::tc_fence_before();
-      tc::mbar_arrive(&pds_full[s]);
-      if (i > 0 && !drain_dq(i - 1)) { ok = false; break; }
+      if constexpr (DSOUT) {
+        // stg_full before pds_full: a thread can reach tile i+1's stg_full arrival only after the dV / dK
+        // MMAs of tile i, i.e. after every thread's pds_full (and so stg_full) arrival for tile i
+        tc::mbar_arrive(stg_full);
+        tc::mbar_arrive(&pds_full[s]);
+        if (ew == 0) {
+          if (!tc::mbar_wait(stg_full, (uint32_t)(i & 1), p.err)) { ok = false; break; }
+          tc::tma_store_3d(&tmDQ, smem + C::OFF_DS + s * C::PT_BYTES, i * C::BQ, k0, bh);
+          tc::bulk_commit();
+          // the store of tile i-1 has read its buffer: the dS^T of tile i+1 may be written there
+          tc::bulk_wait_read1();
+          if (i > 0) tc::mbar_arrive(&pds_empty[s ^ 1]);
+        }
+      } else {
+        tc::mbar_arrive(&pds_full[s]);
+        if (i > 0 && !drain_dq(i - 1)) { ok = false; break; }
+      }
     }
-    if (ok && ntile > 0) ok = drain_dq(ntile - 1);
+    if constexpr (!DSOUT) {
+      if (ok && ntile > 0) ok = drain_dq(ntile - 1);
+    }
     if (ew == 0) tc::bulk_wait0();
     // ---------------- dK, dV epilogue: group g writes d columns [32g, 32g+32) ----------------
     if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
@@ -996,11 +1019,48 @@ bool attn_tc_bwd_eligible(const b2_attn_args* a) {
   return true;
 }
 
-// workspace = fp32 dQ accumulator [B*H][sq_pad/64][D][64] followed by (lse*log2e, delta) [B*H][sq_pad]
+// dS^T [B*H][Sk][sq_pad] bf16 stays in L2 between the backward kernel and the dQ GEMM up to this size
+constexpr uint64_t kDsOutMaxBytes = 64ull << 20;
+
+// The dS-out form pays a separate GEMM launch (~10 us at B1 H16 S1024) to take the dQ^T MMA and its fp32
+// traffic out of the key-tile CTAs. Measured (graphs of back-to-back fwd+bwd, B1 H16 D128): it wins when
+// those CTAs fill at most half the GPU (Sq x Sk = 1024 x 512: 50.0 -> 47.8 us; 4096 x 512: 168 -> 154 us)
+// and loses when they fill it (1024 x 1024: 54.5 -> 56.9 us; 2048 x 2048: even).
+// B2_ATTN_BWD_DSOUT=0 / =1 pins the form (A/B measurements and the tests of both forms).
+bool attn_bwd_dsout(const b2_attn_args* a) {
+  static const int pinned = [] {
+    const char* e = getenv("B2_ATTN_BWD_DSOUT");
+    return e && (e[0] == '0' || e[0] == '1') ? e[0] - '0' : -1;
+  }();
+  const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
+  if (pinned == 0 || a->dq == nullptr ||
+      (uint64_t)(a->B * a->H) * (uint64_t)a->Sk * (uint64_t)sq_pad * 2 > kDsOutMaxBytes)
+    return false;
+  if (pinned == 1) return true;
+  const int64_t key_ctas = a->B * a->H * ((a->Sk + 127) / 128);
+  return 2 * key_ctas <= (int64_t)device_info().sm_count;
+}
+
+// workspace = (dS^T bf16 [B*H][Sk][sq_pad] when attn_bwd_dsout, else the fp32 dQ accumulator
+// [B*H][sq_pad/64][D][64]) followed by (lse*log2e, delta) [B*H][sq_pad]
 uint64_t attn_bwd_ws_bytes(const b2_attn_args* a) {
   if (!attn_tc_bwd_eligible(a)) return 0;
   const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
-  return (uint64_t)(a->B * a->H) * (uint64_t)sq_pad * (uint64_t)(a->D * 4 + 8);
+  const uint64_t per_q = attn_bwd_dsout(a) ? (uint64_t)a->Sk * 2 + 8 : (uint64_t)(a->D * 4 + 8);
+  return (uint64_t)(a->B * a->H) * (uint64_t)sq_pad * per_q;
+}
+
+template <bool DSOUT>
+int set_bwd_smem_attr() {
+  static bool attr = false;
+  if (!attr) {
+    if (int rc = check_cuda(cudaFuncSetAttribute(attn_bwd_tc_kernel<DSOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 BwdCfg::SMEM),
+                            "attn_bwd_tc attr"))
+      return rc;
+    attr = true;
+  }
+  return 0;
 }
 
 int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
@@ -1008,18 +1068,17 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   if (!a->workspace || ((uintptr_t)a->workspace & 15))
     return fail(B2_ERR_ARG, "attn_bwd: a 16-byte aligned workspace of b2_attn_bwd_workspace_bytes() is required");
   using C = BwdCfg;
-  static bool attr = false;
-  if (!attr) {
-    if (int rc = check_cuda(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM),
-                            "attn_bwd_tc attr"))
-      return rc;
-    attr = true;
-  }
+  const bool dsout = attn_bwd_dsout(a);
+  if (int rc = dsout ? set_bwd_smem_attr<true>() : set_bwd_smem_attr<false>()) return rc;
+  const int64_t BH = a->B * a->H;
   const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
-  float* dq_acc = (float*)a->workspace;
-  float2* lsed = reinterpret_cast<float2*>(dq_acc + a->B * a->H * a->D * sq_pad);
+  float* dq_acc = (float*)a->workspace;                                 // !dsout
+  __nv_bfloat16* ds_t = (__nv_bfloat16*)a->workspace;                   // dsout
+  float2* lsed = dsout ? reinterpret_cast<float2*>(ds_t + BH * a->Sk * sq_pad)
+                       : reinterpret_cast<float2*>(dq_acc + BH * a->D * sq_pad);
   {
-    dim3 grid((unsigned)(sq_pad / 64), (unsigned)(a->B * a->H), 2);
+    // z = 1: (lse, delta) blocks only; z = 2 adds the blocks that zero the dQ accumulator
+    dim3 grid((unsigned)(sq_pad / 64), (unsigned)BH, dsout ? 1u : 2u);
     if (int rc = launch_pdl("attn_bwd_prep", attn_bwd_prep, grid, dim3(256), 0, st, (const __nv_bfloat16*)a->o,
                             (const __nv_bfloat16*)a->d_o, (const float*)a->lse, lsed, dq_acc, (int64_t)a->H,
                             (int64_t)a->Sq, sq_pad, a->o_s[0], a->o_s[1], a->o_s[2], a->do_s[0], a->do_s[1],
@@ -1027,9 +1086,16 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
       return rc;
   }
   CUtensorMap tq, tk, tv, tdo, tdq;
-  {
+  if (dsout) {
+    // dS^T as [BH][Sk][sq_pad] bf16, written in 64-query x 128-key boxes (the swizzled shared-memory tile)
+    const uint64_t dims[3] = {(uint64_t)sq_pad, (uint64_t)a->Sk, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)sq_pad * 2, (uint64_t)a->Sk * (uint64_t)sq_pad * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    if (!make_tmap(&tdq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ds_t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return fail(B2_ERR_ARG, "attn_bwd_tc: dS tensor map rejected");
+  } else {
     // dQ accumulator as [B*H*sq_pad/64*D rows][64 fp32], reduced into in 128 x 32 boxes
-    const uint64_t dims[2] = {64, (uint64_t)(a->B * a->H * (sq_pad / 64) * 128)};
+    const uint64_t dims[2] = {64, (uint64_t)(BH * (sq_pad / 64) * 128)};
     const uint64_t strides[1] = {256};
     const uint32_t box[2] = {32, 128};
     if (!make_tmap(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dq_acc, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -1057,13 +1123,31 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   for (int i = 0; i < 3; ++i) p.dk_s[i] = a->dk_s[i], p.dv_s[i] = a->dv_s[i];
   p.err = device_error_ptr();
   {
-    dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)(a->B * a->H));
-    if (int rc = launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv, tdo, tdq, tdk, tdv, p,
-                            (const float2*)lsed, sq_pad))
-      return rc;
+    dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)BH);
+    int rc = dsout ? launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel<true>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv,
+                                tdo, tdq, tdk, tdv, p, (const float2*)lsed, sq_pad)
+                   : launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel<false>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv,
+                                tdo, tdq, tdk, tdv, p, (const float2*)lsed, sq_pad);
+    if (rc) return rc;
   }
-  if (a->dq) {
-    dim3 grid((unsigned)(sq_pad / 32), (unsigned)(a->B * a->H));
+  if (dsout) {
+    // dQ[b, h] = scale * dS[b, h] K[b, h]: A = dS (Sq x Sk) read through dS^T (M-major), B = K (Sk x D,
+    // N-major), one batched tensor-core GEMM over the heads of each batch entry
+    for (int64_t b = 0; b < a->B; ++b) {
+      b2_gemm_args g{};
+      g.a = ds_t + b * a->H * a->Sk * sq_pad;
+      g.b = (const __nv_bfloat16*)a->k + b * a->k_s[0];
+      g.c = (__nv_bfloat16*)a->dq + b * a->dq_s[0];
+      g.M = a->Sq, g.N = a->D, g.K = a->Sk, g.batch = a->H;
+      g.a_sb = a->Sk * sq_pad, g.a_sm = 1, g.a_sk = sq_pad;
+      g.b_sb = a->k_s[1], g.b_sk = a->k_s[2], g.b_sn = 1;
+      g.c_sb = a->dq_s[1], g.c_sm = a->dq_s[2], g.c_sn = 1;
+      g.alpha = a->scale, g.beta = 0.f;
+      g.dtype = B2_BF16;
+      if (int rc = b2_gemm(&g, st)) return rc;
+    }
+  } else if (a->dq) {
+    dim3 grid((unsigned)(sq_pad / 32), (unsigned)BH);
     if (int rc = launch_pdl("attn_dq_convert", attn_dq_convert, grid, dim3(256), 0, st, (const float*)dq_acc,
                             (__nv_bfloat16*)a->dq, (int64_t)a->H, (int64_t)a->Sq, sq_pad, a->dq_s[0], a->dq_s[1],
                             a->dq_s[2], a->scale))
