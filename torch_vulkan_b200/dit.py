@@ -6,9 +6,12 @@ the reference repository): hidden 2048, 16 heads x 128, self-attention + cross-a
 of width 1024, GELU MLP 2048 -> 8192 -> 2048, adaLN-modulated (affine-free) LayerNorm, LoRA rank 16 /
 alpha 16 on the q/k/v/o linears of both attentions (the module layout of tests/anima_on_vk.py:43-48 of the
 reference), every base linear frozen as int8 with a per-output-row fp32 scale. The hot operators run on
-this package's kernels: int8 linears on the fused dequant GEMM (`b2::int8_linear_fwd/dx`), LoRA projections
-on `mm/addmm`, attention on the fused tcgen05 SDPA, LayerNorm on the row kernels, AdamW(foreach=False) on
-`addcmul_/addcdiv_/lerp_`.
+this package's kernels: int8 linears on the fused dequant GEMM (`b2::int8_linear_fwd/dx`) with the LoRA
+up-projection as one more reduction block of it (`tv.int8_lora_linear`; the rank-r down-projection and the
+LoRA weight gradients on `mm`), the MLP with GELU and its derivative in the int8 GEMM epilogues
+(`tv.int8_mlp`), attention on the fused tcgen05 SDPA, LayerNorm on the row kernels, AdamW(foreach=False) on
+`addcmul_/addcdiv_/lerp_` or the multi-tensor AdamW kernel. `DiTStack.enable_block_swap` streams the frozen
+weights of the last blocks from pinned host memory (torch_vulkan_b200.offload).
 """
 
 from __future__ import annotations
@@ -17,6 +20,7 @@ import math
 
 import torch
 import torch.nn as nn
+import torch.utils.checkpoint
 import torch.nn.functional as F
 
 import torch_vulkan_b200 as tv
@@ -144,14 +148,32 @@ class DiTBlock(nn.Module):
 
 
 class DiTStack(nn.Module):
-    def __init__(self, blocks=1, seed=0, device="cuda", **kw):
+    def __init__(self, blocks=1, seed=0, device="cuda", checkpoint=False, **kw):
         super().__init__()
         self.blocks = nn.ModuleList([DiTBlock(seed=seed + i, device=device, **kw) for i in range(blocks)])
+        self.checkpoint = checkpoint
+        self.offloader = None
 
     def forward(self, x, text, cond):
         for b in self.blocks:
-            x = b(x, text, cond)
+            if self.checkpoint:
+                x = torch.utils.checkpoint.checkpoint(b, x, text, cond, use_reentrant=False)
+            else:
+                x = b(x, text, cond)
         return x
+
+    def enable_block_swap(self, blocks_to_swap, ring_size=2):
+        """Keep the frozen int8 weights of the last `blocks_to_swap` blocks in pinned host memory and stream
+        them through `ring_size` device slots (torch_vulkan_b200.offload); turns on activation checkpointing,
+        which the swap needs for the backward."""
+        from .offload import BlockSwapConfig, create_offloader
+
+        dev = next(self.parameters()).device
+        cfg = BlockSwapConfig(device=dev, supports_backward=True, h2d_only=True, ring_size=ring_size)
+        self.checkpoint = True
+        self.offloader = create_offloader("block", self.blocks, len(self.blocks), blocks_to_swap, cfg)
+        self.offloader.prepare_block_devices_before_forward(self.blocks)
+        return self.offloader
 
     def lora_parameters(self):
         return [p for n, p in self.named_parameters() if "lora_" in n]
