@@ -108,6 +108,11 @@ struct TcParams {
   const void* lora_b;
   int64_t lora_b_ld;
   int lora_r, k_total;
+  // split-K reduced inside a thread-block cluster (bf16 kernel, 128-column tiles): kcl > 1 CTAs of a
+  // cluster each take one K slice of the same tile, leave their fp32 partial tile in shared memory and
+  // sum a share of its rows across the cluster through distributed shared memory; no workspace and no
+  // second kernel (the partial/gemm_splitk_reduce form above needs both)
+  int kcl;
 };
 
 enum : int { EPI_NONE = 0, EPI_GELU = 1, EPI_GELU_BWD = 2 };
@@ -234,6 +239,11 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
   // both CTAs of a pair walk the same work items (pair index = blockIdx.x / CG)
   const uint32_t rank = CG == 2 ? tc::cluster_ctarank() : 0u;
   const int unit0 = (int)blockIdx.x / CG, nunits = (int)gridDim.x / CG;
+  // cluster split-K: CTA `krank` of cluster c takes the single work item (split krank, tile c)
+  const bool kc = DEQ == 0 && CG == 1 && BN == 128 && MSUB == 1 && p.kcl > 1;
+  const uint32_t krank = kc ? tc::cluster_ctarank() : 0u;
+  const int w0 = kc ? (int)krank * total_tiles + (int)blockIdx.x / p.kcl : unit0;
+  const int wstep = kc ? total_work : nunits;
   // leader-side barrier addresses as seen from this CTA (its own shared::cta addresses when CG == 1)
   auto leader_bar = [&](uint64_t* bar) -> uint32_t {
     return CG == 2 ? tc::mapa_shared(tc::smem_u32(bar), 0u) : tc::smem_u32(bar);
@@ -302,7 +312,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
       int issued[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       bool ok = true;
       const uint32_t full0 = leader_bar(&full[0]);  // the leader's full[s] is full0 + 8 * s
-      for (int t = unit0; t < total_work && ok; t += nunits) {
+      for (int t = w0; t < total_work && ok; t += wstep) {
         int m0, n0, b, kb0, kb1;
         tile_coords(t, m0, n0, b);
         k_range(t, kb0, kb1);
@@ -390,7 +400,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
       int it = 0;
       int gk = 0;  // K blocks consumed so far (B ring position)
       bool ok = true;
-      for (int t = unit0; t < total_work && ok; t += nunits, ++it) {
+      for (int t = w0; t < total_work && ok; t += wstep, ++it) {
         int kb0, kb1;
         k_range(t, kb0, kb1);
         const int acc = it % NACC;
@@ -456,11 +466,35 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     const bool bias_row = p.has_bias && p.bias_sm == 0 && (p.batch == 1 || p.bias_sb == 0) && p.bias_sn == 1 &&
                           (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
     const uint32_t tempty0 = leader_bar(&tempty[0]);  // pairs: the leader's tempty[a] is tempty0 + 8 * a
-    for (int t = unit0; t < total_work; t += nunits, ++it) {
+    for (int t = w0; t < total_work; t += wstep, ++it) {
       const int acc = it % NACC;
       int m0, n0, b;
       tile_coords(t, m0, n0, b);
       m0 += (int)rank * C::BMT;  // pairs: this CTA's TMEM holds its own BMT rows of the pair tile
+      if (kc) {
+        // cluster split-K: this CTA's fp32 partial tile goes into the stage ring, idle now that the
+        // CTA's single work item is done ([BMT rows][BN + 4] floats, 16-byte aligned rows);
+        // the cluster sums it after the final CTA barrier
+        if (!wait_bar(&tfull[acc], (it / NACC) & 1) || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        float* red = reinterpret_cast<float*>(smem);
+        const int ncols = (int)(p.N - n0 < BN ? p.N - n0 : BN);
+        for (int cc = 0; cc < ncols; cc += 32) {  // warp-uniform
+          uint32_t r[32];
+          __syncwarp();
+          tc::tmem_ld32(tbase + (uint32_t)(acc * C::ACC_COLS + cc) + ((uint32_t)(q * 32) << 16), r);
+          tc::tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(red + (q * 32 + lane) * (BN + 4) + cc);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                                 __uint_as_float(r[4 * j + 3]));
+        }
+        continue;
+      }
       if (bias_row) {
         const OutT* bsrc = (const OutT*)p.bias + n0;
         for (int c = lane; c < BN / 8; c += 32) {
@@ -685,7 +719,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
       uint32_t rph = 0;
       int issued[4] = {0, 0, 0, 0};
       bool ok = true;
-      for (int t = unit0; t < total_work && ok; t += nunits) {
+      for (int t = w0; t < total_work && ok; t += wstep) {
         int m0, n0, b, kb0, kb1;
         tile_coords(t, m0, n0, b);
         k_range(t, kb0, kb1);
@@ -724,7 +758,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     float sc[IPT];
     const uint32_t bready0 = leader_bar(&bready[0]);  // pairs: the leader's bready[i] is bready0 + 8 * i
     bool ok = true;
-    for (int t = unit0; t < total_work && ok; t += nunits) {
+    for (int t = w0; t < total_work && ok; t += wstep) {
       int m0, n0, b, kb0, kb1;
       tile_coords(t, m0, n0, b);
       k_range(t, kb0, kb1);
@@ -860,6 +894,50 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
   __syncthreads();
   // pairs: neither CTA frees its TMEM or leaves while the other may still arrive on its barriers
   if (CG == 2) tc::cluster_sync();
+  if (kc) {
+    // every CTA's partial tile is in its shared memory (barrier.cluster arrive.release / wait.acquire);
+    // CTA krank sums rows [krank * rows, (krank + 1) * rows) over the kcl partials in rank order
+    // (deterministic) through distributed shared memory and writes them to C with alpha and the bias
+    tc::cluster_sync();
+    if (warp >= 2 && warp < 6 && !*abort_flag) {
+      using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      int m0, n0, b;
+      tile_coords(w0, m0, n0, b);
+      const int ncols = (int)(p.N - n0 < BN ? p.N - n0 : BN);
+      const int rows = (C::BMT + p.kcl - 1) / p.kcl;
+      const int r0 = (int)krank * rows, r1 = r0 + rows < C::BMT ? r0 + rows : C::BMT;
+      uint32_t src[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) src[k] = tc::mapa_shared(tc::smem_u32(smem), (uint32_t)(k < p.kcl ? k : 0));
+      // thread = (row, 4 columns): eight 16-byte loads (one per cluster rank) in flight at once
+      const int nc4 = (ncols + 3) >> 2;
+      for (int e = (int)threadIdx.x - 64; e < (r1 - r0) * nc4; e += 128) {
+        const int rr = r0 + e / nc4, col = (e - (e / nc4) * nc4) * 4;
+        const int64_t row = m0 + rr;
+        if (row >= p.M) continue;
+        const uint32_t off = (uint32_t)((rr * (BN + 4) + col) * 4);
+        float4 part[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k < p.kcl) part[k] = tc::ld_shared_cluster_v4(src[k] + off);
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (k < p.kcl) sum[0] += part[k].x, sum[1] += part[k].y, sum[2] += part[k].z, sum[3] += part[k].w;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (col + j >= ncols) break;
+          float v = p.alpha * sum[j];
+          if (p.has_bias) v += p.beta * to_f32(((const OutT*)p.bias)[row * p.bias_sm + (n0 + col + j) * p.bias_sn]);
+          OutT o;
+          if constexpr (BF16) o = __float2bfloat16_rn(v);
+          else o = __float2half_rn(v);
+          ((OutT*)p.c)[row * p.c_sm + (n0 + col + j) * p.c_sn] = o;
+        }
+      }
+    }
+    tc::cluster_sync();  // no CTA leaves while another may still read its partial
+  }
   if (warp == 1) {
     __syncwarp();
     tc::tc_fence_after();
@@ -908,6 +986,28 @@ int launch_kernel(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMa
     attr_set = true;
   }
   const int tiles = p.m_tiles * p.n_tiles * (int)p.batch * p.ksplit;
+  if (CG == 1 && p.kcl > 1) {
+    // cluster split-K: one CTA per (tile, K slice), the kcl slices of a tile in one cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)tiles);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)p.kcl, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+    cfg.attrs = at, cfg.numAttrs = 1;
+    cudaError_t e;
+    {
+      LaunchScope ls("gemm_tc_bn128_kcluster", st);
+      e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc_, *th, p);
+    }
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail_cuda(e, "gemm_tc_bn128_kcluster");
+    }
+    return after_launch("gemm_tc_bn128_kcluster");
+  }
   if (CG == 2) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(2 * std::min(tiles, max_pairs)));
@@ -1021,12 +1121,63 @@ TileChoice pick_tile(int64_t M, int64_t N, int64_t batch) {
   return best;
 }
 
+// How many clusters of ks CTAs of the bf16 128x128 kernel the GPU holds at once (cached per ks).
+int kcluster_capacity(int ks) {
+  static int cap[9] = {0};
+  if (ks < 2 || ks > 8) return 0;
+  if (cap[ks] == 0) {
+    using C = Cfg<128, 0, 1, 1>;
+    auto kern = gemm_tc_kernel<128, true, 0, 1, 1>;
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(ks * 64));
+      cfg.blockDim = dim3(C::THREADS);
+      cfg.dynamicSmemBytes = C::SMEM;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = (unsigned)ks, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+      cfg.attrs = at, cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    (void)cudaGetLastError();
+    cap[ks] = n > 0 ? n : -1;
+  }
+  return cap[ks] > 0 ? cap[ks] : 0;
+}
+
+// Split-K reduced inside a cluster (TcParams::kcl), opt-in with B2_GEMM_KCLUSTER=1: GEMMs with few 128x128
+// output tiles and a long K (the LoRA down-projections and weight gradients: N or M = 16-64) whose
+// splitk_plan split fits a portable cluster (<= 8) take it as clusters of K slices that sum their tile
+// through distributed shared memory, without a workspace or a second kernel. Measured against the default
+// workspace + gemm_splitk_reduce form (graphs of back-to-back calls): 1024x2048x48 8.85 -> 7.73 us,
+// 4096x2048x48 10.8 -> 10.2, 4096x8192x16 21.6 -> 20.5, but 6144x1024x48 (MN-major A, 48 clusters of 3)
+// 10.4 -> 10.6 and the DiT configs[4] stack 69.9 -> 71.3 ms, so it is not the default.
+bool kcluster_plan(const b2_gemm_args* a, const TileChoice& t, int& ks, int& kps) {
+  static const bool on = [] {
+    const char* e = getenv("B2_GEMM_KCLUSTER");
+    return e && e[0] == '1';
+  }();
+  ks = 1, kps = 0;
+  if (!on || a->batch != 1 || t.bn != 128 || t.msub != 1 || a->K <= 0) return false;
+  const int64_t tiles = ((a->M + BM - 1) / BM) * ((a->N + 127) / 128);
+  const int k_blocks = (int)((a->K + BK - 1) / BK);
+  splitk_plan(tiles, k_blocks, ks, kps);
+  // a split wider than a cluster would have to be capped, losing the parallelism the split is for
+  if (ks <= 1 || ks > 8 || tiles * ks > (int64_t)device_info().sm_count) return false;
+  // every cluster must be resident at once: clusters of ks CTAs of ~210 KB each are placed inside one
+  // GPC, and a split whose clusters need a second wave (measured: 48 clusters of 3, 16 of 8) runs at
+  // half speed, so those keep the workspace form
+  return tiles <= kcluster_capacity(ks);
+}
+
 // Tensor map for the output C (16-bit, unit column stride): boxes of 32 columns x 32 rows with the
 // 64 B swizzle the epilogue's staging tiles use. Sets p.c_tma / p.c3d; leaves them 0 (direct
 // stores) when C's layout cannot be described (strided columns, unaligned rows) or the GEMM writes
 // split-K partials.
 void setup_cmap(CUtensorMap* tm, CUtensorMapDataType dt, TcParams& p) {
   p.c_tma = 0, p.c3d = 0;
+  if (p.kcl > 1) return;  // cluster split-K writes C from the reduction, without a tensor map
   if (p.ksplit > 1) {
     // split-K: the map describes the fp32 partials [ksplit][M][N] instead (32-row x 16-column boxes)
     if (p.batch != 1 || (p.N % 4) || ((uintptr_t)p.partial & 15)) return;
@@ -1093,7 +1244,11 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
   p.alpha = a->alpha, p.beta = a->beta;
   p.err = device_error_ptr();
   p.ksplit = 1, p.kps = p.k_blocks;
-  if (a->batch == 1 && a->workspace) {
+  p.kcl = 0;
+  int kcl_ks, kcl_kps;
+  if (kcluster_plan(a, tc_, kcl_ks, kcl_kps)) {
+    p.ksplit = kcl_ks, p.kps = kcl_kps, p.kcl = kcl_ks;
+  } else if (a->batch == 1 && a->workspace) {
     int ks, kps;
     splitk_plan((int64_t)p.m_tiles * p.n_tiles, p.k_blocks, ks, kps);
     if (ks > 1 && (uint64_t)a->workspace_bytes >= (uint64_t)ks * a->M * a->N * sizeof(float) &&
@@ -1147,7 +1302,7 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
   else
     rc = bf16 ? launch_kernel<128, true, 0, 1>(ta, tb, tcm, p, st, "gemm_tc_bn128")
               : launch_kernel<128, false, 0, 1>(ta, tb, tcm, p, st, "gemm_tc_bn128");
-  if (rc || p.ksplit == 1) return rc;
+  if (rc || p.ksplit == 1 || p.kcl > 1) return rc;
   const int64_t total = a->M * a->N;
   const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)device_info().sm_count * 8);
   LaunchScope ls("gemm_splitk_reduce", st);
@@ -1165,6 +1320,8 @@ int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st) {
 uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a) {
   if (a->batch != 1 || a->K == 0 || !gemm_tc_eligible(a)) return 0;
   const TileChoice t = pick_tile(a->M, a->N, a->batch);
+  int ks_c, kps_c;
+  if (kcluster_plan(a, t, ks_c, kps_c)) return 0;  // reduced inside the cluster: no scratch
   const int64_t BMT = BM * t.msub;
   int ks, kps;
   splitk_plan(((a->M + BMT - 1) / BMT) * ((a->N + t.bn - 1) / t.bn), (int)((a->K + BK - 1) / BK), ks, kps);

@@ -22,12 +22,20 @@ import torch.distributed as dist
 
 
 class BucketedGradAllReduce:
+    """With one process there is nothing to average: no flat buffers are bound, so autograd hands each
+    parameter the gradient tensor it computed (no accumulation kernel per parameter) and `zero_grad`
+    resets `.grad` to None."""
+
     def __init__(self, buckets: Sequence[Sequence[torch.nn.Parameter]], group=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.buckets = [list(b) for b in buckets if len(b) > 0]
         self.flats = []
         self._owner = {}
+        if self.world == 1:
+            self._pending = [0] * len(self.buckets)
+            self._handles = []
+            return
         for bi, params in enumerate(self.buckets):
             dtype, dev = params[0].dtype, params[0].device
             if any(p.dtype != dtype or p.device != dev for p in params):
@@ -74,6 +82,11 @@ class BucketedGradAllReduce:
 
     def zero_grad(self):
         """Clears the flat buffers (one memset per bucket) and re-arms the hooks for the next step."""
+        if self.world == 1:
+            for params in self.buckets:
+                for p in params:
+                    p.grad = None
+            return
         for flat in self.flats:
             flat.zero_()
         self._pending = [len(b) for b in self.buckets]
