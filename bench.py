@@ -275,7 +275,9 @@ def run_ours(args, rank, world, local_rank):
     rows = [r.split("\t") for r in tv.profile().splitlines() if r]
     tv.profile_enable(False)
     prof = {r[0]: (float(r[1]), int(r[2])) for r in rows}
-    kernel_flops = {"attn_bwd_tc": 2.5 * FWD_FLOPS, "attn_fwd_tc": FWD_FLOPS}
+    # the whole backward's FLOPs (2.5x forward) for the kernel that computes dK, dV and dQ; the
+    # dS-to-L2 kernel without the fused dQ phase leaves a fifth of them to a GEMM after it
+    kernel_flops = {"attn_bwd_tc_fusedq": 2.5 * FWD_FLOPS, "attn_bwd_tc": 2.5 * FWD_FLOPS, "attn_fwd_tc": FWD_FLOPS}
     dom = max((n for n in prof if n in kernel_flops), key=lambda n: prof[n][0], default=None)
     roofline = None
     if dom:

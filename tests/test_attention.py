@@ -213,12 +213,13 @@ print("RESULT " + json.dumps({"cases": out, "kernels": kernels, "validation_erro
 """
 
 
-@pytest.mark.parametrize("dsout", ["1", "0"])
-def test_tc_backward_forms_ragged(dsout):
-    """Both forms of the tcgen05 backward at ragged D = 128 shapes (query and key counts off the 64 / 128
-    tiles, B > 1), each pinned by B2_ATTN_BWD_DSOUT and compared with float64: dS^T stored to L2 and one dQ
-    GEMM after the kernel (=1; by default taken when the key-tile CTAs fill at most half the GPU), and the
-    in-kernel dQ^T with fp32 reductions into an L2 accumulator (=0)."""
+@pytest.mark.parametrize("dsout,fusedq", [("1", "1"), ("1", "0"), ("0", "1")])
+def test_tc_backward_forms_ragged(dsout, fusedq):
+    """The forms of the tcgen05 backward at ragged D = 128 shapes (query and key counts off the 64 / 128
+    tiles, B > 1), each pinned by B2_ATTN_BWD_DSOUT / B2_ATTN_BWD_FUSEDQ and compared with float64: dS^T
+    stored to L2 with dQ = scale dS K computed by the same kernel in a second phase (1, 1: the default
+    whenever every key-tile CTA fits on the GPU at once) or by a GEMM after it (1, 0), and the in-kernel
+    dQ^T with fp32 reductions into an L2 accumulator (0)."""
     import json
     import os
     import subprocess
@@ -226,11 +227,15 @@ def test_tc_backward_forms_ragged(dsout):
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", BWD_CHILD.replace("ROOT", repr(root))], capture_output=True,
-                       text=True, timeout=600, cwd=root, env=dict(os.environ, B2_ATTN_BWD_DSOUT=dsout))
+                       text=True, timeout=600, cwd=root,
+                       env=dict(os.environ, B2_ATTN_BWD_DSOUT=dsout, B2_ATTN_BWD_FUSEDQ=fusedq))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("RESULT ")][-1][len("RESULT "):])
     assert res["validation_errors"] == 0
-    assert "attn_bwd_tc" in res["kernels"], res["kernels"]
-    assert ("attn_dq_convert" in res["kernels"]) == (dsout == "0"), res["kernels"]
+    ks = res["kernels"]
+    assert ("attn_dq_convert" in ks) == (dsout == "0"), ks
+    assert ("attn_bwd_tc_fusedq" in ks) == (dsout == "1" and fusedq == "1"), ks
+    if dsout == "1" and fusedq == "0":
+        assert "attn_bwd_tc" in ks and any(k.startswith("gemm_tc") for k in ks), ks
     for B, H, Sq, Sk, eq, ek, ev in res["cases"]:
         assert max(eq, ek, ev) < 2e-2, (dsout, B, H, Sq, Sk, eq, ek, ev)

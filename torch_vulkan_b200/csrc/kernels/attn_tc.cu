@@ -63,6 +63,9 @@ struct AttnTcParams {
   void* dk;
   void* dv;
   int64_t dk_s[3], dv_s[3];
+  // fused dQ (dS-to-L2 form, all key-tile CTAs resident at once): per-(b, h) count of key-tile CTAs whose
+  // dS^T tiles are stored, zeroed by the prep kernel; nullptr: dQ comes from a GEMM after the kernel
+  int* dsready;
 };
 
 // ==================================================================================================
@@ -551,6 +554,22 @@ int attn_simt_bwd_dispatch(const b2_attn_args* a, cudaStream_t st);  // attn_sim
 
 namespace {
 
+// Bounded wait until the global counter reaches `target` (acquire at GPU scope); false (with the error
+// word set) after the wait limit.
+__device__ __forceinline__ bool wait_count(const int* ctr, int target, int* err) {
+  uint64_t t0 = tc::globaltimer();
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if (tc::globaltimer() - t0 > tc::kWaitLimitNs) {
+      if (err) atomicExch(err, tc::kErrMbarTimeout);
+      return false;
+    }
+    __nanosleep(128);
+  }
+}
+
 // ==================================================================================================
 // backward (D = 128): one CTA per (128-key tile, batch*head), walking 64-query tiles; two compute
 // warpgroups split each tile's 64 query columns (elementwise work needs no cross-group reduction)
@@ -592,8 +611,8 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                        const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmDK,
-                       const __grid_constant__ CUtensorMap tmDV, AttnTcParams p, const float2* __restrict__ lsed,
-                       int64_t sq_pad) {
+                       const __grid_constant__ CUtensorMap tmDV, const __grid_constant__ CUtensorMap tmDQO,
+                       AttnTcParams p, const float2* __restrict__ lsed, int64_t sq_pad) {
   using C = BwdCfg;
   constexpr bool BF16 = true;
   extern __shared__ uint8_t smem_raw[];
@@ -615,6 +634,11 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
   uint64_t* stg_full = bar + 12 + 2 * QS;  // dQ^T staging tile written (count 256)
   uint64_t* stg_free = bar + 13 + 2 * QS;  // the bulk reduction of the previous tile has read it
   uint64_t* ptm_empty = bar + 14 + 2 * QS;  // dV / dK MMAs of the previous tile read P^T / dS^T in TMEM
+  // fused dQ (second phase): a 3-stage ring of (dS^T, K) blocks over the idle tile regions, the accumulator
+  uint64_t* p2_full = bar + 15 + 2 * QS;     // [3] dS^T and K block landed
+  uint64_t* p2_empty = bar + 18 + 2 * QS;    // [3] MMAs reading the block done
+  uint64_t* p2_acc = bar + 21 + 2 * QS;      // dQ tile complete in TMEM
+  uint64_t* p2_drained = bar + 22 + 2 * QS;  // dQ tile read out of TMEM (count NEW)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = blockIdx.x * C::BKV;
@@ -640,6 +664,12 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
     tc::mbar_init(stg_full, C::NEW);
     tc::mbar_init(stg_free, 1);
     tc::mbar_init(ptm_empty, 1);
+    for (int i = 0; i < 3; ++i) {
+      tc::mbar_init(&p2_full[i], 1);
+      tc::mbar_init(&p2_empty[i], 1);
+    }
+    tc::mbar_init(p2_acc, 1);
+    tc::mbar_init(p2_drained, C::NEW);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -878,6 +908,13 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
       if (ok && ntile > 0) ok = drain_dq(ntile - 1);
     }
     if (ew == 0) tc::bulk_wait0();
+    if (DSOUT && p.dsready != nullptr && ew == 0) {
+      // this CTA's dS^T stores are complete: publish them to the other CTAs of the head (whose TMA
+      // loads read them in the second phase); also on the error path, so that nobody waits for it
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __threadfence();
+      atomicAdd(&p.dsready[bh], 1);
+    }
     // ---------------- dK, dV epilogue: group g writes d columns [32g, 32g+32) ----------------
     if (ok && tc::mbar_wait(dkv_full, 0, p.err)) {
       tc::tc_fence_after();
@@ -922,6 +959,124 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
   __syncwarp();
   tc::tc_fence_before();
   __syncthreads();
+
+  if constexpr (DSOUT) if (p.dsready != nullptr) {
+    // ---------------- second phase: dQ = scale * dS K for this CTA's 128-query tiles ----------------
+    // Every CTA of the grid is resident (cooperative launch), so the wait for the other key tiles of
+    // the head ends. Query tiles qt = blockIdx.x, blockIdx.x + nkt, ... of the head; the reduction runs
+    // over its nkt 128-key blocks: A = dS (M-major, read through the dS^T buffer in L2), B = K (N-major),
+    // both TMA-loaded in 64-element-wide boxes into a 3-stage ring of 64 KB stages laid over the idle
+    // K / V / Q / dO / dS^T regions; the accumulator reuses dV's TMEM columns (drained above).
+    constexpr int P2S = 3;
+    constexpr int P2_STAGE = 65536;
+    static_assert(P2S * P2_STAGE <= C::OFF_LD, "second-phase ring overlaps the (lse, delta) ring");
+    const int nkt = (int)gridDim.x;
+    const int nqt = (int)((p.Sq + 127) / 128);
+    if (warp == 0) {
+      if (lane == 0) {
+        bool ok = !*abort_flag && wait_count(&p.dsready[bh], nkt, p.err);
+        asm volatile("fence.proxy.async.global;" ::: "memory");  // the TMA loads below see those stores
+        int st = 0, issued[P2S] = {0, 0, 0};
+        uint32_t ph = 0;
+        for (int qt = (int)blockIdx.x; qt < nqt && ok; qt += nkt) {
+          for (int kb = 0; kb < nkt; ++kb) {
+            if (!tc::mbar_wait(&p2_empty[st], ph ^ 1, p.err) || *abort_flag) {
+              ok = false;
+              break;
+            }
+            uint8_t* sa = smem + st * P2_STAGE;
+            tc::mbar_arrive_expect_tx(&p2_full[st], P2_STAGE);
+            tc::tma_load_3d(sa, &tmDQ, &p2_full[st], qt * 128, kb * C::BKV, bh);
+            tc::tma_load_3d(sa + 16384, &tmDQ, &p2_full[st], qt * 128 + 64, kb * C::BKV, bh);
+            tc::tma_load_4d(sa + 32768, &tmK, &p2_full[st], 0, kb * C::BKV, h, b);
+            tc::tma_load_4d(sa + 49152, &tmK, &p2_full[st], 64, kb * C::BKV, h, b);
+            issued[st]++;
+            if (++st == P2S) st = 0, ph ^= 1;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          for (int i = 0; i < P2S; ++i)
+            if (issued[i]) tc::mbar_wait(&p2_full[i], (uint32_t)((issued[i] - 1) & 1), nullptr);
+        }
+      }
+    } else if (warp == 1) {
+      if (lane == 0) {
+        constexpr uint32_t IDESC_P2 = tc::idesc_f16(128, 128, BF16, true, true);  // A, B MN-major
+        int st = 0, tcount = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int qt = (int)blockIdx.x; qt < nqt && ok; qt += nkt, ++tcount) {
+          if (tcount > 0 && !tc::mbar_wait(p2_drained, (uint32_t)((tcount - 1) & 1), p.err)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          for (int kb = 0; kb < nkt; ++kb) {
+            if (!tc::mbar_wait(&p2_full[st], ph, p.err) || *abort_flag) {
+              ok = false;
+              break;
+            }
+            tc::tc_fence_after();
+            const uint32_t sa = tc::smem_u32(smem + st * P2_STAGE);
+            const tc::SDesc ad = tc::sdesc_parts(sa, 16384, 1024);          // dS: two 64-query chunks
+            const tc::SDesc bd = tc::sdesc_parts(sa + 32768, 16384, 1024);  // K: two 64-column chunks
+#pragma unroll
+            for (int k = 0; k < C::BKV / 16; ++k)
+              tc::mma_f16_ss(tbase + C::T_DV, tc::sdesc_at(ad, k * 2048), tc::sdesc_at(bd, k * 2048), IDESC_P2,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+            tc::mma_commit(&p2_empty[st]);
+            if (++st == P2S) st = 0, ph ^= 1;
+          }
+          if (ok) tc::mma_commit(p2_acc);
+        }
+        if (!ok) *abort_flag = 1;
+      }
+    } else {
+      // warp (group g, quarter): 32 query rows x 32 d columns per tile, through a per-warp 2 KB staging
+      // box in the idle dQ^T staging region and one TMA store (boxes wholly past Sq are skipped)
+      const int g = (warp - 2) >> 2, quarter = warp & 3;
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      uint8_t* buf = smem + C::OFF_STG + (warp - 2) * 2048;
+      int tcount = 0;
+      for (int qt = (int)blockIdx.x; qt < nqt; qt += nkt, ++tcount) {
+        if (!tc::mbar_wait(p2_acc, (uint32_t)(tcount & 1), p.err) || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        uint32_t v[32];
+        __syncwarp();
+        tc::tmem_ld32(tbase + C::T_DV + g * 32 + lane_off, v);
+        tc::tmem_wait_ld();
+        tc::reg_fence32(v);
+        tc::tc_fence_before();
+        tc::mbar_arrive(p2_drained);
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          w[e] = pack2(__uint_as_float(v[2 * e]) * p.scale, __uint_as_float(v[2 * e + 1]) * p.scale, BF16);
+        if (lane == 0) tc::bulk_wait_read0();  // the previous tile's store has read the staging box
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          *reinterpret_cast<uint4*>(buf + lane * 64 + ((e ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        tc::fence_async_shared();
+        __syncwarp();
+        const int64_t r0 = (int64_t)qt * 128 + quarter * 32;
+        if (lane == 0 && r0 < p.Sq) {
+          tc::tma_store_4d(&tmDQO, buf, g * 32, (int32_t)r0, h, b);
+          tc::bulk_commit();
+        }
+      }
+      if (lane == 0) tc::bulk_wait0();
+    }
+    __syncwarp();
+    tc::tc_fence_before();
+    __syncthreads();
+  }
+
   if (warp == 1) {
     __syncwarp();
     tc::tc_fence_after();
@@ -933,11 +1088,13 @@ __global__ void __launch_bounds__(BwdCfg::THREADS, 1)
 // (+inf, 0) for padding rows, and zero the tile of the fp32 dQ accumulator [bh][q/64][d][64].
 __global__ void __launch_bounds__(256) attn_bwd_prep(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ d_o,
                                                      const float* __restrict__ lse, float2* __restrict__ lsed,
-                                                     float* __restrict__ dq_acc, int64_t H, int64_t Sq, int64_t sq_pad,
-                                                     int64_t o0, int64_t o1, int64_t o2, int64_t g0, int64_t g1, int64_t g2) {
+                                                     float* __restrict__ dq_acc, int* __restrict__ dsready, int64_t H,
+                                                     int64_t Sq, int64_t sq_pad, int64_t o0, int64_t o1, int64_t o2,
+                                                     int64_t g0, int64_t g1, int64_t g2) {
   tc::pdl_wait();
   tc::pdl_trigger();
   const int64_t bh = blockIdx.y, b = bh / H, h = bh % H;
+  if (dsready && blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0) dsready[bh] = 0;  // fused-dQ counter
   const int64_t q0 = (int64_t)blockIdx.x * 64;
   if (blockIdx.z == 1) {  // the zeroing blocks run beside the delta blocks
     float4* acc = reinterpret_cast<float4*>(dq_acc + (bh * (sq_pad / 64) + blockIdx.x) * (128 * 64));
@@ -1027,6 +1184,19 @@ constexpr uint64_t kDsOutMaxBytes = 64ull << 20;
 // those CTAs fill at most half the GPU (Sq x Sk = 1024 x 512: 50.0 -> 47.8 us; 4096 x 512: 168 -> 154 us)
 // and loses when they fill it (1024 x 1024: 54.5 -> 56.9 us; 2048 x 2048: even).
 // B2_ATTN_BWD_DSOUT=0 / =1 pins the form (A/B measurements and the tests of both forms).
+// When every key-tile CTA fits on the GPU at once (one CTA per SM), the dQ GEMM runs inside the backward
+// kernel instead, as a second phase after the CTAs of a head have stored their dS^T tiles (cooperative
+// launch: all CTAs resident, so the wait for the head's other CTAs ends); B2_ATTN_BWD_FUSEDQ=0 keeps the
+// separate GEMM.
+bool attn_bwd_fusedq(const b2_attn_args* a) {
+  static const bool off = [] {
+    const char* e = getenv("B2_ATTN_BWD_FUSEDQ");
+    return e && e[0] == '0';
+  }();
+  const int64_t key_ctas = a->B * a->H * ((a->Sk + 127) / 128);
+  return !off && device_info().coop_launch && key_ctas <= (int64_t)device_info().sm_count;
+}
+
 bool attn_bwd_dsout(const b2_attn_args* a) {
   static const int pinned = [] {
     const char* e = getenv("B2_ATTN_BWD_DSOUT");
@@ -1036,18 +1206,21 @@ bool attn_bwd_dsout(const b2_attn_args* a) {
   if (pinned == 0 || a->dq == nullptr ||
       (uint64_t)(a->B * a->H) * (uint64_t)a->Sk * (uint64_t)sq_pad * 2 > kDsOutMaxBytes)
     return false;
-  if (pinned == 1) return true;
+  if (pinned == 1 || attn_bwd_fusedq(a)) return true;
   const int64_t key_ctas = a->B * a->H * ((a->Sk + 127) / 128);
   return 2 * key_ctas <= (int64_t)device_info().sm_count;
 }
 
-// workspace = (dS^T bf16 [B*H][Sk][sq_pad] when attn_bwd_dsout, else the fp32 dQ accumulator
-// [B*H][sq_pad/64][D][64]) followed by (lse*log2e, delta) [B*H][sq_pad]
+// workspace = (dS^T bf16 [B*H][Sk][sq_pad] and, after the (lse, delta) pairs, one int per (b, h) for the
+// fused form, when attn_bwd_dsout; else the fp32 dQ accumulator [B*H][sq_pad/64][D][64]) with
+// (lse*log2e, delta) [B*H][sq_pad] after it
 uint64_t attn_bwd_ws_bytes(const b2_attn_args* a) {
   if (!attn_tc_bwd_eligible(a)) return 0;
   const int64_t sq_pad = (a->Sq + 63) / 64 * 64;
-  const uint64_t per_q = attn_bwd_dsout(a) ? (uint64_t)a->Sk * 2 + 8 : (uint64_t)(a->D * 4 + 8);
-  return (uint64_t)(a->B * a->H) * (uint64_t)sq_pad * per_q;
+  const bool ds = attn_bwd_dsout(a);
+  const uint64_t per_q = ds ? (uint64_t)a->Sk * 2 + 8 : (uint64_t)(a->D * 4 + 8);
+  const uint64_t extra = ds ? ((uint64_t)(a->B * a->H) * 4 + 15) / 16 * 16 : 0;
+  return (uint64_t)(a->B * a->H) * (uint64_t)sq_pad * per_q + extra;
 }
 
 template <bool DSOUT>
@@ -1076,11 +1249,13 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   __nv_bfloat16* ds_t = (__nv_bfloat16*)a->workspace;                   // dsout
   float2* lsed = dsout ? reinterpret_cast<float2*>(ds_t + BH * a->Sk * sq_pad)
                        : reinterpret_cast<float2*>(dq_acc + BH * a->D * sq_pad);
+  const bool fused = dsout && attn_bwd_fusedq(a);
+  int* dsready = fused ? reinterpret_cast<int*>(lsed + BH * sq_pad) : nullptr;
   {
     // z = 1: (lse, delta) blocks only; z = 2 adds the blocks that zero the dQ accumulator
     dim3 grid((unsigned)(sq_pad / 64), (unsigned)BH, dsout ? 1u : 2u);
     if (int rc = launch_pdl("attn_bwd_prep", attn_bwd_prep, grid, dim3(256), 0, st, (const __nv_bfloat16*)a->o,
-                            (const __nv_bfloat16*)a->d_o, (const float*)a->lse, lsed, dq_acc, (int64_t)a->H,
+                            (const __nv_bfloat16*)a->d_o, (const float*)a->lse, lsed, dq_acc, dsready, (int64_t)a->H,
                             (int64_t)a->Sq, sq_pad, a->o_s[0], a->o_s[1], a->o_s[2], a->do_s[0], a->do_s[1],
                             a->do_s[2]))
       return rc;
@@ -1107,12 +1282,14 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
       !make_bhsd_map(&tdo, a->d_o, a->do_s, a->B, a->H, a->Sq, 128, true, 64))
     return fail(B2_ERR_ARG, "attn_bwd_tc: tensor map rejected");
   // dK / dV (when requested) are written by TMA stores of 32 x 32 boxes
-  CUtensorMap tdk, tdv;
+  CUtensorMap tdk, tdv, tdqo;
   memset(&tdk, 0, sizeof(tdk));
   memset(&tdv, 0, sizeof(tdv));
+  memset(&tdqo, 0, sizeof(tdqo));
   if ((a->dk && !make_bhsd_map(&tdk, a->dk, a->dk_s, a->B, a->H, a->Sk, 128, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) ||
-      (a->dv && !make_bhsd_map(&tdv, a->dv, a->dv_s, a->B, a->H, a->Sk, 128, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
-    return fail(B2_ERR_ARG, "attn_bwd_tc: dK / dV tensor map rejected");
+      (a->dv && !make_bhsd_map(&tdv, a->dv, a->dv_s, a->B, a->H, a->Sk, 128, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) ||
+      (fused && !make_bhsd_map(&tdqo, a->dq, a->dq_s, a->B, a->H, a->Sq, 128, true, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return fail(B2_ERR_ARG, "attn_bwd_tc: dK / dV / dQ tensor map rejected");
   AttnTcParams p{};
   p.B = a->B, p.H = a->H, p.Sq = a->Sq, p.Sk = a->Sk;
   p.scale = a->scale;
@@ -1122,12 +1299,36 @@ int attn_tc_bwd(const b2_attn_args* a, cudaStream_t st) {
   p.dk = a->dk, p.dv = a->dv;
   for (int i = 0; i < 3; ++i) p.dk_s[i] = a->dk_s[i], p.dv_s[i] = a->dv_s[i];
   p.err = device_error_ptr();
+  p.dsready = dsready;
+  if (fused) {
+    // all CTAs resident at once (the second phase waits for the head's other key tiles)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a->Sk + 127) / 128), (unsigned)BH);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at, cfg.numAttrs = 1;
+    cudaError_t e;
+    {
+      LaunchScope ls("attn_bwd_tc_fusedq", st);
+      e = cudaLaunchKernelEx(&cfg, attn_bwd_tc_kernel<true>, tq, tk, tv, tdo, tdq, tdk, tdv, tdqo, p,
+                             (const float2*)lsed, sq_pad);
+    }
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail_cuda(e, "attn_bwd_tc_fusedq");
+    }
+    return after_launch("attn_bwd_tc_fusedq");
+  }
   {
     dim3 grid((unsigned)((a->Sk + 127) / 128), (unsigned)BH);
     int rc = dsout ? launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel<true>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv,
-                                tdo, tdq, tdk, tdv, p, (const float2*)lsed, sq_pad)
+                                tdo, tdq, tdk, tdv, tdqo, p, (const float2*)lsed, sq_pad)
                    : launch_pdl("attn_bwd_tc", attn_bwd_tc_kernel<false>, grid, dim3(C::THREADS), C::SMEM, st, tq, tk, tv,
-                                tdo, tdq, tdk, tdv, p, (const float2*)lsed, sq_pad);
+                                tdo, tdq, tdk, tdv, tdqo, p, (const float2*)lsed, sq_pad);
     if (rc) return rc;
   }
   if (dsout) {

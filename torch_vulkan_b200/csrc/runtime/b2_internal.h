@@ -22,6 +22,7 @@ struct DeviceInfo {
   int smem_optin = 0;  // max dynamic shared memory per block (bytes)
   int cc_major = 0, cc_minor = 0;
   bool tcgen05 = false;  // sm_100a kernels usable (compute capability 10.0)
+  bool coop_launch = false;  // cooperative launches (every CTA of a grid resident at once) supported
 };
 const DeviceInfo& device_info();  // initialises on first use; device < 0 when no GPU
 int ensure_init();

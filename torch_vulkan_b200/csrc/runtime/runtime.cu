@@ -113,6 +113,7 @@ const DeviceInfo& device_info() {
     g_dev.cc_major = p.major;
     g_dev.cc_minor = p.minor;
     g_dev.tcgen05 = (p.major == 10 && p.minor == 0);
+    g_dev.coop_launch = p.cooperativeLaunch != 0;
   });
   return g_dev;
 }
