@@ -183,7 +183,9 @@ typedef struct b2_gemm_args {
 int b2_gemm(const b2_gemm_args* args, b2_stream_t stream);
 /* Scratch bytes b2_gemm would use for these arguments (0: none). */
 uint64_t b2_gemm_workspace_bytes(const b2_gemm_args* args);
-/* Which kernel b2_gemm would pick for these arguments: 0 = SIMT, 1 = tcgen05. */
+/* Which kernel b2_gemm would pick for these arguments: 0 = SIMT, 1 = tcgen05, 2 = skinny (bf16/f16 with one
+ * output dimension <= 64 and a multiple of 8 and K >= 256: mma.sync with the reduction split across the
+ * warps of a CTA, one launch and no workspace). */
 int b2_gemm_path(const b2_gemm_args* args);
 
 /* Weight-only int8 dequant. Replaces dequant_int8_vk (csrc/ops_quant.cpp:34-59, kernel

@@ -2,9 +2,9 @@
 DiT block: one of M, N is 16-64, K is long): each CTA of a cluster computes one K slice of a 128x128 tile
 and the cluster sums the fp32 partials through distributed shared memory, with no workspace and no second
 kernel. Checked against float64 in both forms — the cluster reduction (opt-in, B2_GEMM_KCLUSTER=1) and
-the default workspace + gemm_splitk_reduce form (=0), each pinned in a child process — over K-major and
-MN-major operands, ragged M/N, bias with alpha/beta, and splits wider than a cluster (which keep the
-workspace form)."""
+the workspace + gemm_splitk_reduce form (=0), each pinned in a child process with the skinny kernel (which
+serves these shapes by default) switched off — over K-major and MN-major operands, ragged M/N, bias with
+alpha/beta, and splits wider than a cluster (which keep the workspace form)."""
 
 import json
 import os
@@ -56,7 +56,7 @@ print("RESULT " + json.dumps({"cases": out, "kernels": kernels, "validation_erro
 @pytest.mark.parametrize("kcluster", ["1", "0"])
 def test_split_k_forms_match_float64(kcluster):
     r = subprocess.run([sys.executable, "-c", CHILD.replace("ROOT", repr(ROOT))], capture_output=True, text=True,
-                       timeout=600, cwd=ROOT, env=dict(os.environ, B2_GEMM_KCLUSTER=kcluster))
+                       timeout=600, cwd=ROOT, env=dict(os.environ, B2_GEMM_KCLUSTER=kcluster, B2_GEMM_SKINNY="0"))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("RESULT ")][-1][len("RESULT "):])
     assert res["validation_errors"] == 0
@@ -70,9 +70,10 @@ def test_split_k_forms_match_float64(kcluster):
         assert err < 4e-3, (kcluster, m, k, n, ta, tb, bias, err)
 
 
-def test_default_split_keeps_its_workspace():
-    """By default (no B2_GEMM_KCLUSTER) a split-K GEMM asks for its fp32 partial scratch: the LoRA
-    down-projection shape of the stacked q/k/v group (1024 x 48 x 2048, 8 K slices)."""
+def test_workspace_only_for_tcgen05_splits():
+    """A split-K tcgen05 GEMM asks for its fp32 partial scratch (1024 x 128 x 8192: 8 output tiles, 16 K
+    slices of 8 blocks); the LoRA weight-gradient shape of the stacked q/k/v group at 1024 tokens
+    (2048 x 48 x 1024) goes to the skinny kernel and asks for none."""
     import ctypes
 
     import torch_vulkan_b200  # noqa: F401
@@ -91,7 +92,9 @@ def test_default_split_keeps_its_workspace():
     assert lib.b2rt_init() == 0
     g = GemmArgs()
     g.a, g.b, g.c = 256, 256, 256  # only the layout matters here; nothing is launched
-    g.M, g.N, g.K, g.batch = 1024, 48, 2048, 1
-    g.a_sm, g.a_sk, g.b_sk, g.b_sn, g.c_sm, g.c_sn = 2048, 1, 48, 1, 48, 1
+    g.M, g.N, g.K, g.batch = 1024, 128, 8192, 1
+    g.a_sm, g.a_sk, g.b_sk, g.b_sn, g.c_sm, g.c_sn = 8192, 1, 128, 1, 128, 1
     g.alpha, g.dtype = 1.0, 1  # B2_BF16
-    assert lib.b2_gemm_workspace_bytes(ctypes.byref(g)) == 8 * 1024 * 48 * 4
+    assert lib.b2_gemm_workspace_bytes(ctypes.byref(g)) == 16 * 1024 * 128 * 4
+    g.M, g.N, g.K, g.a_sm, g.b_sk, g.c_sm = 2048, 48, 1024, 1024, 48, 48
+    assert lib.b2_gemm_workspace_bytes(ctypes.byref(g)) == 0

@@ -258,7 +258,9 @@ def coop_caps() -> int:
 
 
 def gemm_path(a: torch.Tensor, b: torch.Tensor) -> str:
-    return "tcgen05" if int(torch.ops.b2.gemm_path(a, b)) == 1 else "simt"
+    """Which kernel serves mm(a, b): "tcgen05", "skinny" (one output dimension <= 64, mma.sync with the
+    K loop split across warps) or "simt"."""
+    return {1: "tcgen05", 2: "skinny"}.get(int(torch.ops.b2.gemm_path(a, b)), "simt")
 
 
 # ---- int8 weight-only quantisation ---------------------------------------------------------------

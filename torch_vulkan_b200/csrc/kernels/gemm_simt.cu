@@ -11,6 +11,8 @@ namespace b2 {
 
 int gemm_tc_launch(const b2_gemm_args* a, cudaStream_t st);  // gemm_tc.cu
 bool gemm_tc_eligible(const b2_gemm_args* a);
+bool gemm_skinny_applies(const b2_gemm_args* a);                // gemm_skinny.cu
+int gemm_skinny_launch(const b2_gemm_args* a, cudaStream_t st);
 uint64_t gemm_tc_workspace_bytes(const b2_gemm_args* a);  // gemm_tc.cu
 
 namespace {
@@ -125,11 +127,13 @@ using namespace b2;
 
 extern "C" uint64_t b2_gemm_workspace_bytes(const b2_gemm_args* a) {
   if (!a || a->force_simt || ensure_init()) return 0;
+  if (a->K > 0 && gemm_skinny_applies(a)) return 0;
   return a->K > 0 ? gemm_tc_workspace_bytes(a) : 0;
 }
 
 extern "C" int b2_gemm_path(const b2_gemm_args* a) {
   if (!a || a->force_simt) return 0;
+  if (a->K > 0 && gemm_skinny_applies(a)) return 2;
   return gemm_tc_eligible(a) ? 1 : 0;
 }
 
@@ -145,6 +149,7 @@ extern "C" int b2_gemm(const b2_gemm_args* a, b2_stream_t stream) {
   if (!a->c || (a->K > 0 && (!a->a || !a->b))) return fail(B2_ERR_ARG, "gemm: null pointer");
   if (a->has_bias && !a->bias) return fail(B2_ERR_ARG, "gemm: has_bias with null bias");
   cudaStream_t s = (cudaStream_t)stream;
+  if (!a->force_simt && a->K > 0 && gemm_skinny_applies(a)) return gemm_skinny_launch(a, s);
   if (!a->force_simt && a->K > 0 && gemm_tc_eligible(a)) return gemm_tc_launch(a, s);
   switch (a->dtype) {
     case B2_F32: return simt_launch<float>(a, s);
