@@ -40,7 +40,9 @@ struct SkCfg {
   static constexpr int A_ELEMS = BM * (kKB + kPad) > kKB * (BM + kPad) ? BM * (kKB + kPad) : kKB * (BM + kPad);
   static constexpr int B_ELEMS = NP * (kKB + kPad) > kKB * (NP + kPad) ? NP * (kKB + kPad) : kKB * (NP + kPad);
   static constexpr int STAGE_BYTES = (A_ELEMS + B_ELEMS) * 2;
-  static constexpr int WARP_BYTES = 2 * STAGE_BYTES;
+  // K blocks in flight per warp: four when eight warps' rings fit in 200 KB, else three
+  static constexpr int STAGES = kWarps * 4 * STAGE_BYTES <= 200 * 1024 ? 4 : 3;
+  static constexpr int WARP_BYTES = STAGES * STAGE_BYTES;
   static constexpr int RED_BYTES = kWarps * BM * NP * 4;
   static constexpr int SMEM = kWarps * WARP_BYTES > RED_BYTES ? kWarps * WARP_BYTES : RED_BYTES;
   static_assert(STAGE_BYTES % 16 == 0, "stages must keep 16-byte alignment");
@@ -152,16 +154,19 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_skinny_kernel(SkParams p) {
     for (int j = 0; j < NT; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.f;
 
   const int mi = lane >> 3, r8 = lane & 7;  // ldmatrix: matrix index and row within it
-  int st = 0;
-  if (warp < nkb) load(0, warp);
-  for (int kb = warp; kb < nkb; kb += kWarps) {
-    if (kb + kWarps < nkb) {
-      load(st ^ 1, kb + kWarps);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+  constexpr int S = C::STAGES;
+  // this warp's K blocks are warp, warp + 8, ...; block i of them lands in stage i % S, S - 1 ahead of use
+  // (an empty group is committed where there is no block, so the wait count stays uniform)
+#pragma unroll
+  for (int i = 0; i < S - 1; ++i) {
+    const int kb = warp + i * kWarps;
+    if (kb < nkb) load(i, kb);
+    else cp_async_commit();
+  }
+  for (int i = 0, kb = warp; kb < nkb; ++i, kb += kWarps) {
+    cp_async_wait<S - 2>();
     __syncwarp();
+    const int st = i % S;
     const T* sa = reinterpret_cast<const T*>(wbase + st * C::STAGE_BYTES);
     const T* sb = sa + C::A_ELEMS;
 #pragma unroll
@@ -191,8 +196,11 @@ __global__ void __launch_bounds__(kWarps * 32) gemm_skinny_kernel(SkParams p) {
       }
     }
     __syncwarp();  // every lane is done reading this stage before it is refilled
-    st ^= 1;
+    const int kn = kb + (S - 1) * kWarps;  // into the stage read in the previous iteration
+    if (kn < nkb) load((i + S - 1) % S, kn);
+    else cp_async_commit();
   }
+  cp_async_wait<0>();
 
   // the eight warps' partial tiles are summed through shared memory (the stages are idle now)
   __syncthreads();
@@ -285,10 +293,11 @@ bool normalise(const b2_gemm_args* a, SkParams& p) {
 
 // Taken for bf16/f16 GEMMs whose narrow dimension is <= 64 (a multiple of 8), with 256 <= K <= 1024 and a
 // wide dimension of at most 2048: there it beats the tcgen05 kernel's split-K form (graphs of back-to-back
-// calls: 2048x1024x48 with M-major A 8.7 -> 7.1 us). Each warp keeps one K block in flight while it
-// computes the previous one and every CTA re-reads all of B, so longer reductions and wider outputs are
-// latency-bound here (1024x6144x48 10.5 -> 27.5 us, 4096x2048x48 10.7 -> 13.1 us) and stay on the tcgen05
-// kernel. B2_GEMM_SKINNY=0 never takes it, =1 takes it for every supported layout up to K x 64 x 2 <= 1.5 MB.
+// calls: 2048x1024x48 with M-major A 8.7 -> 6.5 us). Every CTA re-reads all of B through cp.async, whose
+// outstanding requests per SM cap it near 30 GB/s per SM whatever the pipeline depth (two and three K
+// blocks in flight per warp measured the same), so longer reductions and wider outputs stay on the TMA-fed
+// tcgen05 kernel (1024x6144x48 10.5 us there, 26 us here; 4096x2048x48 10.8 against 13.2).
+// B2_GEMM_SKINNY=0 never takes it, =1 takes it for every supported layout up to K x 64 x 2 <= 1.5 MB.
 bool gemm_skinny_applies(const b2_gemm_args* a) {
   static const int pinned = [] {
     const char* e = getenv("B2_GEMM_SKINNY");
