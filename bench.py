@@ -386,10 +386,11 @@ def e2e_pipelined(host, dev, steps, world):
 
     run(16)  # warm-up (allocates the pinned output buffers and brings the host link out of its idle state)
     torch.cuda.synchronize()
-    # three timed repetitions; the median is reported (host-link throughput on these shared hosts varies
-    # from one repetition to the next when neighbouring GPUs move data)
+    # seven timed repetitions; the median is reported and all are listed (host-link throughput on these
+    # shared hosts varies from one repetition to the next when neighbouring GPUs move data: one of three
+    # repetitions measured 3.3 ms against 0.42 ms for the others)
     reps = []
-    for _ in range(3):
+    for _ in range(7):
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -403,7 +404,7 @@ def e2e_pipelined(host, dev, steps, world):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         reps.append(t.item())
-    return sorted(reps)[1], reps
+    return sorted(reps)[len(reps) // 2], reps
 
 
 def run_dit(dev, world, blocks, tokens, steps, warmup):

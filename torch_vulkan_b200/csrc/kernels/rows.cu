@@ -423,6 +423,22 @@ __global__ void __launch_bounds__(256) ln_fwd_reg(const T* __restrict__ x, const
   const int rpb = blockDim.x / GROUP;
   const int t = threadIdx.x % GROUP;
   const float invD = 1.f / (float)D;
+  // rows of up to two chunks per thread keep this thread's weight and bias columns in registers, loaded
+  // once before the first row, so no load sits between a row's reductions and its stores
+  constexpr bool HOIST = NCH <= 2;
+  float wh[HOIST ? NCH : 1][V], bh[HOIST ? NCH : 1][V];
+  if constexpr (HOIST) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t idx = ((int64_t)c * GROUP + t) * V;
+#pragma unroll
+      for (int i = 0; i < V; ++i) wh[c][i] = 1.f, bh[c][i] = 0.f;
+      if (idx < D) {
+        if (w) VecIO<T, V>::load(w + idx, wh[c]);
+        if (b) VecIO<T, V>::load(b + idx, bh[c]);
+      }
+    }
+  }
   for (int64_t row = (int64_t)blockIdx.x * rpb + threadIdx.x / GROUP; row - threadIdx.x / GROUP < rows;
        row += (int64_t)gridDim.x * rpb) {
     const bool active = row < rows;
@@ -455,15 +471,21 @@ __global__ void __launch_bounds__(256) ln_fwd_reg(const T* __restrict__ x, const
     for (int c = 0; c < NCH; ++c) {
       int64_t idx = ((int64_t)c * GROUP + t) * V;
       if (idx < D) {
-        float o[V], wv[V], bv[V];
-        if (w) VecIO<T, V>::load(w + idx, wv);
-        if (b) VecIO<T, V>::load(b + idx, bv);
+        float o[V];
+        if constexpr (HOIST) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          float r = (v[c][i] - mu) * rs;
-          if (w) r *= wv[i];
-          if (b) r += bv[i];
-          o[i] = r;
+          for (int i = 0; i < V; ++i) o[i] = fmaf((v[c][i] - mu) * rs, wh[c][i], bh[c][i]);
+        } else {
+          float wv[V], bv[V];
+          if (w) VecIO<T, V>::load(w + idx, wv);
+          if (b) VecIO<T, V>::load(b + idx, bv);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            float r = (v[c][i] - mu) * rs;
+            if (w) r *= wv[i];
+            if (b) r += bv[i];
+            o[i] = r;
+          }
         }
         VecIO<T, V>::store(y + row * D + idx, o);
       }
