@@ -381,6 +381,30 @@ typedef struct b2_adamw_args {
 } b2_adamw_args;
 int b2_adamw_step(const b2_adamw_args* args, b2_stream_t stream);
 
+/* Mean squared error between two contiguous tensors of n elements (the training loss of the DiT LoRA step,
+ * F.mse_loss(x.float(), t.float()); replaces the fp32 mse_loss the reference's autocast policy routes to,
+ * csrc/shim.cpp:414, as its training tests call it, tests/test_ops_ew.py:333), computed from the 16-bit (or fp32) inputs with fp32 arithmetic and a
+ * fixed summation order (deterministic):
+ *   forward:  *loss = sum((x - t)^2) / n  (fp32), in two launches; `partial` is scratch of
+ *             b2_mse_loss_workspace_bytes(n) bytes
+ *   backward: grad_x = 2 (x - t) * (*grad_loss) / n, rounded to the dtype of x, in one launch
+ * grad_loss and loss are device pointers to fp32 scalars (n = 0 gives a NaN loss, the mean over nothing). dtype: F32, BF16 or F16
+ * (x, t, grad_x). */
+typedef struct b2_mse_args {
+  const void* x;
+  const void* t;
+  float* loss;
+  void* grad_x;
+  const float* grad_loss;
+  float* partial;
+  int64_t n;
+  int32_t dtype;
+  int32_t pad_;
+} b2_mse_args;
+int b2_mse_loss_fwd(const b2_mse_args* args, b2_stream_t stream);
+int b2_mse_loss_bwd(const b2_mse_args* args, b2_stream_t stream);
+uint64_t b2_mse_loss_workspace_bytes(int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,7 +20,8 @@ def test_header_declares_the_expected_families():
     names = declared_functions()
     for must in ("b2rt_init", "b2rt_last_error", "b2rt_alloc", "b2rt_free", "b2_malloc", "b2_free", "b2_gemm",
                  "b2_int8_gemm", "b2_dequant_int8", "b2_attn_fwd", "b2_attn_bwd", "b2_softmax_fwd", "b2_softmax_bwd",
-                 "b2_layernorm_fwd", "b2_layernorm_bwd", "b2_ew_ternary", "b2_adamw_step"):
+                 "b2_layernorm_fwd", "b2_layernorm_bwd", "b2_ew_ternary", "b2_adamw_step", "b2_mse_loss_fwd",
+                 "b2_mse_loss_bwd"):
         assert must in names, must
 
 

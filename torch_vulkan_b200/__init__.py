@@ -330,6 +330,27 @@ def int8_lora_linear(x, q, scale, bias, a, b):
     return _Int8LoRA.apply(x, q, scale, bias, a, b)
 
 
+class _MseLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, t):
+        ctx.save_for_backward(x, t)
+        return torch.ops.b2.mse_loss_fwd(x, t)
+
+    @staticmethod
+    def backward(ctx, g):
+        x, t = ctx.saved_tensors
+        gx = torch.ops.b2.mse_loss_bwd(g, x, t) if ctx.needs_input_grad[0] else None
+        gt = (-torch.ops.b2.mse_loss_bwd(g, x, t)) if ctx.needs_input_grad[1] else None
+        return gx, gt
+
+
+def mse_loss(x: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+    """F.mse_loss(x.float(), t.float()) (mean reduction, fp32 result) computed from x and t in their own
+    16-bit dtype: two launches forward, one backward, no fp32 copies, a fixed summation order. The
+    gradient is returned in x's dtype."""
+    return _MseLoss.apply(x, t)
+
+
 class _Int8GeluMLP(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, q1, s1, b1, q2, s2, b2):

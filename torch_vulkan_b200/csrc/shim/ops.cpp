@@ -617,6 +617,49 @@ at::Tensor b2_dequant_int8_op(const at::Tensor& q0, const at::Tensor& scale0, at
   return out;
 }
 
+// =============================== MSE loss ==========================================================
+
+int mse_dtype(const at::Tensor& x, const at::Tensor& t, const char* what) {
+  TORCH_CHECK(x.is_cuda() && t.is_cuda(), what, ": CUDA tensors expected");
+  TORCH_CHECK(x.scalar_type() == t.scalar_type(), what, ": input and target must share a dtype");
+  TORCH_CHECK(x.sizes() == t.sizes(), what, ": input and target must have the same shape");
+  const auto st = x.scalar_type();
+  TORCH_CHECK(st == at::kFloat || st == at::kBFloat16 || st == at::kHalf, what, ": float32, bfloat16 or float16");
+  return dtype_code(st);
+}
+
+// mean((x - t)^2) in fp32 from the inputs' own dtype (F.mse_loss(x.float(), t.float())), deterministic
+at::Tensor b2_mse_loss_fwd_op(const at::Tensor& x0, const at::Tensor& t0) {
+  const int dt = mse_dtype(x0, t0, "mse_loss");
+  c10::cuda::CUDAGuard guard(x0.device());
+  at::Tensor x = x0.contiguous(), t = t0.contiguous();
+  at::Tensor loss = at::empty({}, x.options().dtype(at::kFloat));
+  const uint64_t wsb = b2_mse_loss_workspace_bytes(x.numel());
+  at::Tensor ws = at::empty({(int64_t)std::max<uint64_t>(wsb / 4, 1)}, x.options().dtype(at::kFloat));
+  b2_mse_args a{};
+  a.x = x.data_ptr(), a.t = t.data_ptr(), a.loss = loss.data_ptr<float>(), a.partial = ws.data_ptr<float>();
+  a.n = x.numel(), a.dtype = dt;
+  b2_check(b2_mse_loss_fwd(&a, cur_stream()), "mse_loss");
+  count("b2::mse_loss_fwd");
+  return loss;
+}
+
+// d loss / d x = 2 (x - t) * grad / n, in x's dtype
+at::Tensor b2_mse_loss_bwd_op(const at::Tensor& grad0, const at::Tensor& x0, const at::Tensor& t0) {
+  const int dt = mse_dtype(x0, t0, "mse_loss_backward");
+  c10::cuda::CUDAGuard guard(x0.device());
+  at::Tensor x = x0.contiguous(), t = t0.contiguous();
+  at::Tensor grad = grad0.to(at::kFloat).contiguous();
+  TORCH_CHECK(grad.numel() == 1, "mse_loss_backward: a scalar upstream gradient is expected");
+  at::Tensor gx = at::empty_like(x);
+  b2_mse_args a{};
+  a.x = x.data_ptr(), a.t = t.data_ptr(), a.grad_x = gx.data_ptr(), a.grad_loss = grad.data_ptr<float>();
+  a.n = x.numel(), a.dtype = dt;
+  b2_check(b2_mse_loss_bwd(&a, cur_stream()), "mse_loss_backward");
+  count("b2::mse_loss_bwd");
+  return gx;
+}
+
 // split-K scratch for the int8 GEMM (GEMMs with too few output tiles to fill the GPU) from the
 // caching allocator; the returned tensor keeps it alive for the call
 at::Tensor int8_workspace(b2_int8_gemm_args& g, const at::Tensor& like) {
@@ -877,6 +920,8 @@ TORCH_LIBRARY(b2, m) {
   m.def("int8_linear_dx_gelu(Tensor dy, Tensor q, Tensor scale, Tensor h) -> Tensor");
   m.def("int8_lora_fwd(Tensor x, Tensor q, Tensor scale, Tensor? bias, Tensor h, Tensor b) -> Tensor");
   m.def("int8_lora_dx(Tensor dy, Tensor q, Tensor scale, Tensor dh, Tensor a) -> Tensor");
+  m.def("mse_loss_fwd(Tensor x, Tensor t) -> Tensor");
+  m.def("mse_loss_bwd(Tensor grad, Tensor x, Tensor t) -> Tensor");
   m.def("adamw_step_(Tensor(a!)[] params, Tensor[] grads, Tensor(b!)[] exp_avgs, Tensor(c!)[] exp_avg_sqs, float lr, "
         "float beta1, float beta2, float eps, float weight_decay, int step) -> ()");
   m.def("set_enabled(bool on) -> ()", &op_set_enabled);
@@ -895,5 +940,7 @@ TORCH_LIBRARY_IMPL(b2, CUDA, m) {
   m.impl("int8_linear_dx_gelu", &b2_int8_linear_dx_gelu);
   m.impl("int8_lora_fwd", &b2_int8_lora_fwd);
   m.impl("int8_lora_dx", &b2_int8_lora_dx);
+  m.impl("mse_loss_fwd", &b2_mse_loss_fwd_op);
+  m.impl("mse_loss_bwd", &b2_mse_loss_bwd_op);
   m.impl("adamw_step_", &b2_adamw_step_op);
 }

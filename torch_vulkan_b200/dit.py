@@ -207,7 +207,8 @@ def make_optimizer(params, lr=1e-4, fused=False):
 
 
 class LoRATrainer:
-    """One LoRA training step of a DiTStack: forward, MSE loss against the target, backward, data-parallel
+    """One LoRA training step of a DiTStack: forward, MSE loss against the target (F.mse_loss(out.float(),
+    target.float()) on the fused loss kernels, tv.mse_loss; target in the output's dtype), backward, data-parallel
     gradient averaging (bucketed per block, overlapped with the backward when torch.distributed is
     initialised), AdamW on the LoRA parameters (per-tensor foreach=False ops, or fused_optimizer=True for
     the multi-tensor kernel)."""
@@ -222,8 +223,7 @@ class LoRATrainer:
         self.opt = make_optimizer(self.params, lr=lr, fused=fused_optimizer)
 
     def step(self, x, text, cond, target):
-        out = self.model(x, text, cond)
-        loss = F.mse_loss(out.float(), target.float())
+        loss = tv.mse_loss(self.model(x, text, cond), target)
         loss.backward()
         self.reducer.wait()
         self.opt.step()
@@ -253,7 +253,7 @@ class LoRATrainer:
         with torch.cuda.graph(graph, capture_error_mode=mode):
             for flat in self.reducer.flats:  # gradients accumulate into the bucket buffers
                 flat.zero_()
-            loss = F.mse_loss(self.model(x, text, cond).float(), target.float())
+            loss = tv.mse_loss(self.model(x, text, cond), target)
             loss.backward()
             self.reducer.wait()  # the captured collectives join the capture stream before it ends
         self._graph = graph  # kept alive with its memory pool (release it before destroying the group)
