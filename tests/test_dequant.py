@@ -110,3 +110,31 @@ def test_int8_linear_equals_dequant_then_linear(tv):
     w = tv.dequant_int8(q.cuda(), s.cuda(), torch.bfloat16)
     two_step = torch.nn.functional.linear(x.cuda(), w, b.cuda()).float()
     assert torch.allclose(fused, two_step, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("M,N,K,layout,bias", [(1, 18432, 2048, 1, True), (1, 100, 16, 1, False), (2, 384, 320, 0, True),
+                                               (3, 520, 144, 1, True), (5, 96, 2048, 0, False), (8, 2048, 4096, 1, True)])
+def test_int8_linear_few_rows_weight_stream(tv, M, N, K, layout, bias):
+    """x with at most 8 rows (the DiT adaLN modulation: one conditioning vector against an int8 [18432,
+    2048] weight) takes the weight-stream kernel instead of a 128-row tensor-core tile: same dequantised
+    weights, fp32 accumulation, against the float64 oracle in the GEMM tolerance; block-64 bf16 scales
+    and per-row fp32 scales, ragged N, K down to one 16-column chunk, x a column slice of a wider tensor."""
+    if layout == 1:
+        x, q, s, b = config1(20 + M, M, N, K)
+    else:
+        q, s = make_int8(N, K, 30 + M)
+        x = rnd_mm((M, K), torch.bfloat16, 31 + M)
+        b = (0.02 * rnd_mm((N,), torch.float32, 32)).to(torch.bfloat16)
+    b = b if bias else None
+    xs = torch.zeros(M, K + 64, dtype=torch.bfloat16)
+    xs[:, 8:8 + K] = x
+    tv.profile_enable(True)
+    try:
+        out = tv.int8_linear(xs.cuda()[:, 8:8 + K], q.cuda(), s.cuda(), None if b is None else b.cuda())
+        torch.cuda.synchronize()
+        kernels = [ln.split("\t")[0] for ln in tv.profile().splitlines() if ln]
+    finally:
+        tv.profile_enable(False)
+    assert "int8_gemv" in kernels
+    gemm_check(out, oracle.int8_linear(x, q, s, b), torch.bfloat16, K)
+    assert tv.validation_errors() == 0

@@ -112,4 +112,27 @@ inline int grid_for(int64_t work_items, int per_block, int max_blocks_per_sm = 8
   return (int)blocks;
 }
 
+// 16 int8 * scale -> 8 words of packed bf16 (one fp32 multiply and one round-to-nearest-even each,
+// the same bits as b2_dequant_int8 for every finite product). The exact int8 -> fp32 step and the
+// scale multiply run as packed two-lane fp32 operations (each lane rounds exactly as the scalar op).
+__device__ __forceinline__ void dequant16(const int4& raw, float s, uint32_t* w) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
+  const float2 ss = make_float2(s, s);
+  const float2 bias = make_float2(-8388736.f, -8388736.f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t u = r[i] ^ 0x80808080u;
+    float2 lo = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)));
+    float2 hi = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)));
+    lo = __fmul2_rn(__fadd2_rn(lo, bias), ss);
+    hi = __fmul2_rn(__fadd2_rn(hi, bias), ss);
+    __nv_bfloat162 blo = __floats2bfloat162_rn(lo.x, lo.y);
+    __nv_bfloat162 bhi = __floats2bfloat162_rn(hi.x, hi.y);
+    w[2 * i] = *reinterpret_cast<uint32_t*>(&blo);
+    w[2 * i + 1] = *reinterpret_cast<uint32_t*>(&bhi);
+  }
+}
+
 }  // namespace b2

@@ -29,6 +29,9 @@
 
 namespace b2 {
 
+bool int8_gemv_applies(const b2_int8_gemm_args* a);  // int8_gemv.cu
+int int8_gemv_launch(const b2_int8_gemm_args* a, cudaStream_t st);
+
 // ---- driver entry point for tensor-map encoding (no -lcuda needed) ------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -182,29 +185,6 @@ __device__ __forceinline__ uint32_t pack_out(float lo, float hi, bool bf16) {
   }
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// 16 int8 * scale -> 8 words of packed bf16 (one fp32 multiply and one round-to-nearest-even each,
-// the same bits as b2_dequant_int8 for every finite product). The exact int8 -> fp32 step and the
-// scale multiply run as packed two-lane fp32 operations (each lane rounds exactly as the scalar op).
-__device__ __forceinline__ void dequant16(const int4& raw, float s, uint32_t* w) {
-  const uint32_t* r = reinterpret_cast<const uint32_t*>(&raw);
-  const float2 ss = make_float2(s, s);
-  const float2 bias = make_float2(-8388736.f, -8388736.f);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t u = r[i] ^ 0x80808080u;
-    float2 lo = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
-                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)));
-    float2 hi = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
-                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)));
-    lo = __fmul2_rn(__fadd2_rn(lo, bias), ss);
-    hi = __fmul2_rn(__fadd2_rn(hi, bias), ss);
-    __nv_bfloat162 blo = __floats2bfloat162_rn(lo.x, lo.y);
-    __nv_bfloat162 bhi = __floats2bfloat162_rn(hi.x, hi.y);
-    w[2 * i] = *reinterpret_cast<uint32_t*>(&blo);
-    w[2 * i + 1] = *reinterpret_cast<uint32_t*>(&bhi);
-  }
 }
 
 template <int BN, bool BF16, int DEQ, int MSUB, int CG>
@@ -1433,6 +1413,7 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
                             "leading dims that are multiples of 8");
   cudaStream_t st = (cudaStream_t)stream;
   if (a->workspace && ((uintptr_t)a->workspace & 15)) return fail(B2_ERR_ARG, "int8_gemm: workspace must be 16-byte aligned");
+  if (int8_gemv_applies(a)) return int8_gemv_launch(a, st);  // a few rows of x: the weight-stream kernel
   b2_int8_gemm_args aa = *a;
   if (!aa.workspace) aa.workspace_bytes = 0;
   const Int8Plan best = int8_plan(&aa);
@@ -1508,7 +1489,7 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
 }
 
 extern "C" uint64_t b2_int8_gemm_workspace_bytes(const b2_int8_gemm_args* a) {
-  if (!a || a->M <= 0 || a->N <= 0 || a->K <= 0 || !device_info().tcgen05) return 0;
+  if (!a || a->M <= 0 || a->N <= 0 || a->K <= 0 || !device_info().tcgen05 || int8_gemv_applies(a)) return 0;
   b2_int8_gemm_args q = *a;
   q.workspace = nullptr, q.workspace_bytes = INT64_MAX;  // the plan a large enough workspace gets
   const Int8Plan pl = int8_plan(&q);
