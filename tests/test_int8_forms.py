@@ -2,7 +2,8 @@
 of a cluster sharing each M = 256 MMA and each dequantising half of the B tile) and single CTAs. The
 launch plan picks a form per shape; B2_INT8_CG=1|2 pins it for a whole process, so each form runs the
 same cases in its own child process: forward with bias (per-row fp32 and block-64 bf16 scales), the
-transposed dX form, ragged edges, and the split-K shapes of the DiT block (fc2 forward, fc1 dX)."""
+transposed dX form, ragged edges, and the split-K shapes of the DiT block (fc2 forward, fc1 dX). Two more
+children pin one pair tile (B2_INT8_TILE) for every shape."""
 
 import json
 import os
@@ -50,9 +51,11 @@ print("RESULT " + json.dumps({"cases": out, "validation_errors": tv.validation_e
 """
 
 
-@pytest.mark.parametrize("cg", ["1", "2"])
-def test_int8_kernel_form_matches_oracle(cg):
+@pytest.mark.parametrize("cg,tile", [("1", None), ("2", None), ("2", "128x1"), ("2", "256x1")])
+def test_int8_kernel_form_matches_oracle(cg, tile):
     env = dict(os.environ, B2_INT8_CG=cg)
+    if tile:  # every shape on one tile form (256 x 128 or 256 x 256 pair tiles, no split-K)
+        env["B2_INT8_TILE"] = tile
     r = subprocess.run([sys.executable, "-c", CHILD.replace("ROOT", repr(ROOT))], capture_output=True, text=True,
                        timeout=600, cwd=ROOT, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
@@ -60,4 +63,4 @@ def test_int8_kernel_form_matches_oracle(cg):
     assert res["validation_errors"] == 0
     for M, N, K, lay, e_f, e_d in res["cases"]:
         # bf16 output rounding only (relative L2 ~1e-3): a wrong B half or a lost K slice is far above
-        assert e_f < 4e-3 and e_d < 4e-3, (cg, M, N, K, lay, e_f, e_d)
+        assert e_f < 4e-3 and e_d < 4e-3, (cg, tile, M, N, K, lay, e_f, e_d)

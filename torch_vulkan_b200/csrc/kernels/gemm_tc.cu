@@ -1325,13 +1325,15 @@ Int8Plan int8_plan(const b2_int8_gemm_args* a) {
   // the B tile, which halves the dequant work and the B operand bytes per CTA; pair tiles are
   // 2 * 128 * msub rows by bn columns and use half as many units of GPU capacity (one per pair).
   // eff: measured relative per-SM rate of each shape (pairs: estimated from their shared-memory bytes
-  // per K block until measured, B2_INT8_CG=1|2 pins the choice for sweeps).
+  // per K block until measured, B2_INT8_CG=1|2 pins the choice for sweeps). The 256 x 128 pair tile
+  // (0.75) takes the M = 1024, N = 2048 and M = 512, N = 4096 shapes of the DiT block, where 256 x 256
+  // pairs leave half the SMs idle: measured 32.2 -> 25.2 us forward, 37.8 -> 27.5 us dX at K = 2048.
   struct Choice { int bn, msub, cg; double eff; };
   const Choice fwd_opts[] = {{256, 2, 2, 1.55}, {176, 2, 2, 1.45}, {256, 1, 2, 1.3}, {128, 2, 2, 1.25},
                              {256, 2, 1, 1.15}, {176, 2, 1, 1.08}, {128, 2, 1, 1.0},  {96, 2, 1, 0.97},
-                             {256, 1, 1, 0.85}, {128, 1, 1, 0.55}};
+                             {256, 1, 1, 0.85}, {128, 1, 2, 0.75},  {128, 1, 1, 0.55}};
   const Choice dx_opts[] = {{256, 2, 2, 1.55}, {256, 1, 2, 1.3}, {128, 2, 2, 1.25}, {256, 2, 1, 1.15},
-                            {128, 2, 1, 1.0},  {256, 1, 1, 0.85}, {128, 1, 1, 0.55}};
+                            {128, 2, 1, 1.0},  {256, 1, 1, 0.85}, {128, 1, 2, 0.75},  {128, 1, 1, 0.55}};
   const int sms = device_info().sm_count > 0 ? device_info().sm_count : 148;
   const int64_t out_cols = a->transpose_w ? a->K : a->N;
   const int64_t red = a->transpose_w ? a->N : a->K;
@@ -1347,7 +1349,7 @@ Int8Plan int8_plan(const b2_int8_gemm_args* a) {
   }();
   Int8Plan best{0, 0, 1, k_blocks, 1};
   double best_score = -1.0;
-  const int nopts = a->transpose_w ? 7 : 10;
+  const int nopts = a->transpose_w ? 8 : 11;
   for (int i = 0; i < nopts; ++i) {
     const Choice c = a->transpose_w ? dx_opts[i] : fwd_opts[i];
     if (forced_cg && c.cg != forced_cg) continue;
@@ -1472,6 +1474,7 @@ extern "C" int b2_int8_gemm(const b2_int8_gemm_args* a, b2_stream_t stream) {
     if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2, 2>(ta, tb, tcm, p, st, pname, &th);
     else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2, 2>(ta, tb, tcm, p, st, pname, &th);
     else if (best.msub == 2) rc = launch_kernel<128, true, 2, 2, 2>(ta, tb, tcm, p, st, pname, &th);
+    else if (BN == 128) rc = launch_kernel<128, true, 2, 1, 2>(ta, tb, tcm, p, st, pname, &th);
     else rc = launch_kernel<256, true, 2, 1, 2>(ta, tb, tcm, p, st, pname, &th);
   } else if (best.msub == 2 && BN == 256) rc = launch_kernel<256, true, 2, 2>(ta, tb, tcm, p, st, name, &th);
   else if (best.msub == 2 && BN == 176) rc = launch_kernel<176, true, 2, 2>(ta, tb, tcm, p, st, name, &th);
