@@ -151,11 +151,16 @@ struct Cfg {
   // tiles (released by the dequant warps as soon as they have converted one, so those loads run
   // ahead of the MMAs) and NB dequantised bf16 B tiles (released by the MMAs).
   static constexpr int STAGE = A_BYTES + (DEQ ? 0 : B_BYTES);
-  static constexpr int NB = DEQ;  // int8: depth of the dequantised B ring (DEQ = 0: the bf16 path)
-  static constexpr int NR = DEQ ? (R_BYTES >= 11264 ? 3 : 4) : 0;  // int8: depth of the raw ring
-  static_assert(CG == 1 || (DEQ && BNC % 8 == 0), "CTA pairs: int8 kernels, B halves of whole 8-row groups");
   // epilogue: per warp one staging buffer (32 rows x 32 16-bit columns) and the tile's bias row
   static constexpr int EPI_BYTES = 4 * 2048 + 4 * 512;
+  // int8: the dequant warps form DQG groups that take alternate K blocks, so that one group's waits,
+  // proxy fence and barrier arrivals overlap the other group's conversion (one group converting every
+  // K block left the MMA waiting on the slowest warp's per-block latency); two groups need four B
+  // buffers and four raw tiles, which every shape whose A ring keeps three stages affords
+  static constexpr int DQG = (DEQ && (224 * 1024 - 4 * B_BYTES - 4 * R_BYTES - EPI_BYTES) / STAGE >= 3) ? 2 : 1;
+  static constexpr int NB = DEQ ? 2 * DQG : 0;  // int8: depth of the dequantised B ring (DEQ = 0: the bf16 path)
+  static constexpr int NR = !DEQ ? 0 : DQG == 2 ? 4 : (R_BYTES >= 11264 ? 3 : 4);  // int8: depth of the raw ring
+  static_assert(CG == 1 || (DEQ && BNC % 8 == 0), "CTA pairs: int8 kernels, B halves of whole 8-row groups");
   static constexpr int BUDGET = 224 * 1024 - NB * B_BYTES - NR * R_BYTES - EPI_BYTES;
   static constexpr int STAGES = BUDGET / STAGE > 8 ? 8 : BUDGET / STAGE;
   static constexpr int OFF_R = STAGES * STAGE;       // int8: the raw ring
@@ -237,12 +242,12 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
     }
     for (int i = 0; i < NB; ++i) {
       // one arrival per dequant warp (of both CTAs of a pair)
-      tc::mbar_init(&bready[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS * CG : 1);
+      tc::mbar_init(&bready[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS / C::DQG * CG : 1);
       tc::mbar_init(&bfree[i], 1);
     }
     for (int i = 0; i < NR; ++i) {
       tc::mbar_init(&rfull[i], 1);
-      tc::mbar_init(&rempty[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS : 1);
+      tc::mbar_init(&rempty[i], C::DEQ_WARPS > 0 ? C::DEQ_WARPS / C::DQG : 1);
     }
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&tfull[i], 1);
@@ -729,12 +734,15 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
   } else if (DEQ && (warp & 3) != 1) {
     // ------------------------------- int8 dequant -------------------------------------------
     const int dw = warp - 6 - (warp > 9 ? 1 : 0) - (warp > 13 ? 1 : 0);  // 0 .. 7
-    const int dt = dw * 32 + lane;                                        // 0 .. NDQ-1
+    constexpr int DQG = C::DQG;
+    constexpr int NDQG = (NDQ > 0 ? NDQ : DQG) / DQG;  // threads of one group
+    const int grp = dw / (C::DEQ_WARPS / DQG);          // this warp's group: K blocks gk with gk % DQG == grp
+    const int dt = (dw % (C::DEQ_WARPS / DQG)) * 32 + lane;  // 0 .. NDQG-1
     int gk = 0;  // K blocks staged so far (B ring position)
     int gr = 0;  // int8 tiles converted so far (raw ring position; the LoRA block has none)
-    constexpr int FIPT = (BNC * 4 + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // forward items per thread
+    constexpr int FIPT = (BNC * 4 + NDQG - 1) / NDQG;  // forward items per thread
     float fsc[FIPT];
-    constexpr int IPT = (64 * (BNC / 16) + (NDQ > 0 ? NDQ : 1) - 1) / (NDQ > 0 ? NDQ : 1);  // transposed items per thread
+    constexpr int IPT = (64 * (BNC / 16) + NDQG - 1) / NDQG;  // transposed items per thread
     float sc[IPT];
     const uint32_t bready0 = leader_bar(&bready[0]);  // pairs: the leader's bready[i] is bready0 + 8 * i
     bool ok = true;
@@ -744,12 +752,14 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
       k_range(t, kb0, kb1);
       n0 += (int)rank * BNC;  // pairs: this CTA dequantises B rows [n0 + rank * BN/2, + BN/2)
       for (int kb = kb0; kb < kb1; ++kb) {
+        const bool lora_blk = kb >= p.k_blocks;
+        const bool mine = DQG == 1 || gk % DQG == grp;
         // forward scales, loaded before the waits so that their latency overlaps them: block-64
-        // scales change with the K block, per-row scales are loaded once per tile
-        if (!p.b_mn && kb < p.k_blocks && (p.scale_layout == 0 || kb == kb0)) {
+        // scales change with the K block, per-row scales are loaded once per tile (by every group)
+        if (!p.b_mn && !lora_blk && ((p.scale_layout == 0 && mine) || (p.scale_layout != 0 && kb == kb0))) {
 #pragma unroll
           for (int u = 0; u < FIPT; ++u) {  // every scale load in flight before the first is used
-            const int i = dt + u * NDQ;
+            const int i = dt + u * NDQG;
             const int64_t gn = (int64_t)n0 + (i >> 2);
             fsc[u] = 0.f;
             if (i < BNC * 4 && gn < p.deq_rows)
@@ -758,13 +768,17 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
                            : reinterpret_cast<const float*>(p.scale)[gn];
           }
         }
+        if (!mine) {  // the other group's K block
+          ++gk;
+          if (!lora_blk) ++gr;
+          continue;
+        }
         const int rs = gr % NR;
-        const bool lora_blk = kb >= p.k_blocks;
         if (p.b_mn && !lora_blk) {
           // transposed form: the scale of reduction row nf = kb * 64 + i, loaded before the waits
 #pragma unroll
           for (int u = 0; u < IPT; ++u) {  // every scale load in flight before the first is used
-            const int e = dt + u * NDQ;
+            const int e = dt + u * NDQG;
             const int i = e / (BNC / 16), qd = e % (BNC / 16);
             const int64_t nf = (int64_t)kb * BK + i;   // n_feat (the reduction index)
             const int64_t kf = (int64_t)n0 + qd * 16;  // first k_feat of the 16
@@ -792,7 +806,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
           // lora_b row n0 + n; transposed: lora_b [r, K], reduction row i of the tile is lora_b row i
           const __nv_bfloat16* lb = reinterpret_cast<const __nv_bfloat16*>(p.lora_b);
           if (!p.b_mn) {
-            for (int e = dt; e < BNC * 8; e += NDQ) {
+            for (int e = dt; e < BNC * 8; e += NDQG) {
               const int n = e >> 3, c = e & 7;  // 16 B chunk c = k 8c..8c+7 of row n
               const int64_t gn = (int64_t)n0 + n;
               uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -800,7 +814,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
               *reinterpret_cast<uint4*>(sb + n * 128 + ((c ^ (n & 7)) << 4)) = v;
             }
           } else {
-            for (int e = dt; e < 64 * (BNC / 8); e += NDQ) {
+            for (int e = dt; e < 64 * (BNC / 8); e += NDQG) {
               const int i = e / (BNC / 8), g8 = e % (BNC / 8);  // reduction row i, output columns 8*g8..
               const int64_t col = (int64_t)n0 + g8 * 8;
               uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -814,7 +828,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
           // 16 B chunk c (k 8c..8c+7) at ((c ^ (n & 7)) * 16).
 #pragma unroll
           for (int u = 0; u < FIPT; ++u) {
-            const int i = dt + u * NDQ;
+            const int i = dt + u * NDQG;
             if (i >= BNC * 4) break;
             const int n = i >> 2, j = i & 3;  // 16 int8 = k 16j..16j+15
             const float s = fsc[u];
@@ -831,7 +845,7 @@ __global__ void __launch_bounds__(Cfg<BN, DEQ, MSUB, CG>::THREADS, 1)
           // chunk j = n_gemm/64 at j*8192, row i at i*128, 16 B granule g at ((g ^ (i & 7)) * 16).
 #pragma unroll
           for (int u = 0; u < IPT; ++u) {
-            const int e = dt + u * NDQ;
+            const int e = dt + u * NDQG;
             if (e >= 64 * (BNC / 16)) break;
             const int i = e / (BNC / 16), qd = e % (BNC / 16);
             const float s = sc[u];
