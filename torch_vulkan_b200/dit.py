@@ -109,11 +109,15 @@ class DiTBlock(nn.Module):
         return stacked_lora_forward(x, getattr(self, f"{name}_q"), getattr(self, f"{name}_scale"),
                                     getattr(self, f"{name}_bias"), mods)
 
-    def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op):
+    def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op, kv=None):
         B, S, _ = xq.shape
         Skv = xkv_k.shape[1]
         # projections that read the same input run as one stacked group (stacked_lora_forward)
-        if xq is xkv_k and xkv_k is xkv_v and qp is self.q:
+        if kv is not None:  # k, v projected ahead on the side stream
+            q = qp(xq)
+            torch.cuda.current_stream(xq.device).wait_stream(self._side)
+            k, v = kv
+        elif xq is xkv_k and xkv_k is xkv_v and qp is self.q:
             q, k, v = self._stacked("qkv", xq, (qp, kp, vp))
         elif xkv_k is xkv_v and kp is self.ck:
             q = qp(xq)
@@ -126,7 +130,27 @@ class DiTBlock(nn.Module):
         o = F.scaled_dot_product_attention(q, k, v)
         return op(o.transpose(1, 2).reshape(B, S, self.h))
 
+    # the text-side k/v projection depends only on the text embeddings: it runs on a side stream, beside the
+    # modulation, the first LayerNorm and the self-attention branch, and autograd runs its backward (the
+    # LoRA gradients of ck/cv) on the same side stream, beside the rest of the block's backward
+    overlap_text_kv = True
+    _side = None
+
+    def _text_kv_ahead(self, text):
+        if not (self.overlap_text_kv and text.is_cuda):
+            return None
+        main = torch.cuda.current_stream(text.device)
+        if self._side is None or self._side.device != text.device:
+            self._side = torch.cuda.Stream(text.device)
+        self._side.wait_stream(main)
+        with torch.cuda.stream(self._side):
+            kv = self._stacked("ckv", text, (self.ck, self.cv))
+        for t in kv:  # consumed on the main stream: keep the allocator from reusing them early
+            t.record_stream(main)
+        return kv
+
     def forward(self, x, text, cond):
+        kv = self._text_kv_ahead(text)
         mod = self.ada(F.silu(cond)).unsqueeze(1).chunk(9, dim=-1)
         sh1, sc1, g1, sh2, sc2, g2, sh3, sc3, g3 = mod
 
@@ -139,7 +163,7 @@ class DiTBlock(nn.Module):
         h = modln(x, sh1, sc1)
         x = torch.addcmul(x, g1, self._attn(h, h, h, self.q, self.k, self.v, self.o))
         h = modln(x, sh2, sc2)
-        x = torch.addcmul(x, g2, self._attn(h, text, text, self.cq, self.ck, self.cv, self.co))
+        x = torch.addcmul(x, g2, self._attn(h, text, text, self.cq, self.ck, self.cv, self.co, kv=kv))
         h = modln(x, sh3, sc3)
         # MLP fc2(gelu(fc1(h))) with the GELU (and its backward) in the int8 GEMM epilogues
         mlp = tv.int8_mlp(h, self.fc1.q, self.fc1.scale, self.fc1.bias, self.fc2.q, self.fc2.scale, self.fc2.bias)

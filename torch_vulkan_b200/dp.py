@@ -34,6 +34,7 @@ class BucketedGradAllReduce:
         self._owner = {}
         if self.world == 1:
             self._pending = [0] * len(self.buckets)
+            self._streams = [set() for _ in self.buckets]
             self._handles = []
             return
         for bi, params in enumerate(self.buckets):
@@ -46,6 +47,7 @@ class BucketedGradAllReduce:
                 self._owner[p] = bi
                 p.register_post_accumulate_grad_hook(self._on_grad)
         self._pending = [len(b) for b in self.buckets]
+        self._streams = [set() for _ in self.buckets]
         self._handles = []
         self._bind()
 
@@ -60,8 +62,17 @@ class BucketedGradAllReduce:
     def _on_grad(self, p):
         bi = self._owner[p]
         self._pending[bi] -= 1
+        if p.is_cuda:  # the stream this gradient was accumulated on (autograd runs each op on its forward's)
+            self._streams[bi].add(torch.cuda.current_stream(p.device))
         if self._pending[bi] == 0 and self.world > 1:
             flat = self.flats[bi]
+            # the collective is ordered after the current stream only: make that stream wait for every other
+            # stream that accumulated into this bucket (a block whose branches ran on two streams)
+            if self._streams[bi]:
+                cur = torch.cuda.current_stream(flat.device)
+                for s in self._streams[bi]:
+                    if s != cur:
+                        cur.wait_stream(s)
             backend = dist.get_backend(self.group)
             if backend == "nccl":
                 self._handles.append(dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=self.group, async_op=True))
@@ -90,6 +101,7 @@ class BucketedGradAllReduce:
         for flat in self.flats:
             flat.zero_()
         self._pending = [len(b) for b in self.buckets]
+        self._streams = [set() for _ in self.buckets]
         self._bind()
 
 
