@@ -63,18 +63,86 @@ class LoRAInt8Linear(nn.Module):
         return tv.int8_lora_linear(x, self.base.q, self.base.scale, self.base.bias, self.lora_down, b)
 
 
-def stacked_lora_forward(x, q, scale, bias, mods):
-    """LoRAInt8Linear.forward of several modules that read the same input x, with their frozen int8
-    bases stacked in (q, scale, bias): one down-projection GEMM over the stacked A_i, then one int8 GEMM
-    whose last reduction block adds the up-projection over the block-diagonal B_i (backward: one dX GEMM
-    that also adds dh @ A, and one GEMM each for dh, dA and dB, instead of one of each per module).
+class LoRAGroup:
+    """The LoRA matrices of several LoRAInt8Linear modules that read the same input, kept in stacked storage:
+    the modules' lora_down Parameters are row blocks of one [G*r, in] matrix and their lora_up Parameters
+    row blocks of one [G*N, r] matrix (every Parameter stays contiguous, so optimizers see nothing new),
+    plus the block-diagonal [G*N, G*r] up-projection the int8 GEMM's LoRA block reads, refreshed in place
+    from the stacked up matrices by one copy per forward. No per-step cat / block_diag / gradient copies."""
+
+    def __init__(self, mods):
+        self.mods = list(mods)
+        self.g = len(mods)
+        self.r = mods[0].lora_down.shape[0]
+        self.n = mods[0].lora_up.shape[0]
+        self.scale = mods[0].scale
+        assert all(m.lora_down.shape[0] == self.r and m.lora_up.shape == (self.n, self.r) and m.scale == self.scale
+                   and m.lora_down.shape[1] == mods[0].lora_down.shape[1] for m in mods)
+        with torch.no_grad():
+            self.a = torch.cat([m.lora_down.detach() for m in mods], 0)   # [G*r, in]
+            self.b = torch.cat([m.lora_up.detach() for m in mods], 0)     # [G*N, r]
+            self.b_bd = torch.zeros(self.g * self.n, self.g * self.r, dtype=self.b.dtype, device=self.b.device)
+        for i, m in enumerate(mods):
+            m.lora_down = nn.Parameter(self.a[i * self.r:(i + 1) * self.r])
+            m.lora_up = nn.Parameter(self.b[i * self.n:(i + 1) * self.n])
+
+    def refresh(self):
+        """b_bd's diagonal blocks <- B_i * alpha / r (one strided copy; the off-diagonal blocks stay zero)."""
+        with torch.no_grad():
+            diag = self.b_bd.view(self.g, self.n, self.g, self.r).diagonal(dim1=0, dim2=2)  # [N, r, G]
+            diag.copy_(self.b.view(self.g, self.n, self.r).permute(1, 2, 0))
+            if self.scale != 1.0:
+                diag.mul_(self.scale)
+
+
+class _StackedInt8LoRA(torch.autograd.Function):
+    """y = x W~^T + bias + (x A^T) B_bd^T for a LoRAGroup (W~ the stacked frozen int8 bases); gradients for x
+    and for every module's lora_down / lora_up, the latter as contiguous row blocks of two stacked GEMM
+    results (one strided copy pulls the diagonal blocks out of dB)."""
+
+    @staticmethod
+    def forward(ctx, x, q, scale, bias, grp, *params):
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        h = torch.mm(x2, grp.a.t())  # the rank-r down-projections of every module, one GEMM
+        y = torch.ops.b2.int8_lora_fwd(x2, q, scale, bias, h, grp.b_bd)
+        ctx.save_for_backward(x2, q, scale, h)
+        ctx.grp, ctx.x_shape = grp, x.shape
+        return y.view(*x.shape[:-1], q.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, q, scale, h = ctx.saved_tensors
+        grp = ctx.grp
+        gy2 = gy.reshape(-1, gy.shape[-1])
+        if not gy2.is_contiguous():
+            gy2 = gy2.contiguous()
+        dh = torch.mm(gy2, grp.b_bd)  # [rows, G*r] (alpha / r included)
+        gx = None
+        if ctx.needs_input_grad[0]:  # dy W~ + dh A in one GEMM
+            gx = torch.ops.b2.int8_lora_dx(gy2, q, scale, dh, grp.a).view(ctx.x_shape)
+        ga = torch.mm(dh.t(), x2)  # [G*r, in]: row block i is module i's lora_down gradient
+        gb_full = torch.mm(gy2.t(), h)  # [G*N, G*r]: only the diagonal blocks are used
+        gb = torch.empty_like(grp.b)
+        gb.view(grp.g, grp.n, grp.r).copy_(gb_full.view(grp.g, grp.n, grp.g, grp.r).diagonal(dim1=0, dim2=2).permute(2, 0, 1))
+        if grp.scale != 1.0:
+            gb.mul_(grp.scale)
+        gdown = [ga[i * grp.r:(i + 1) * grp.r] for i in range(grp.g)]
+        gup = [gb[i * grp.n:(i + 1) * grp.n] for i in range(grp.g)]
+        return (gx, None, None, None, None, *gdown, *gup)
+
+
+def stacked_lora_forward(x, q, scale, bias, grp: LoRAGroup):
+    """LoRAInt8Linear.forward of the modules of a LoRAGroup (they read the same input x), with their frozen
+    int8 bases stacked in (q, scale, bias): one down-projection GEMM over the stacked A_i, then one int8
+    GEMM whose last reduction block adds the up-projection over the block-diagonal B_i (backward: one dX
+    GEMM that also adds dh @ A, and one GEMM each for dh, dA and dB, instead of one of each per module).
     Returns one [..., out_i] view per module."""
-    a = torch.cat([m.lora_down for m in mods], 0)
-    b = torch.block_diag(*[m.lora_up for m in mods])
-    if mods[0].scale != 1.0:
-        b = b * mods[0].scale
-    out = tv.int8_lora_linear(x, q, scale, bias, a, b)
-    return out.split([m.base.q.shape[0] for m in mods], dim=-1)
+    grp.refresh()
+    params = [m.lora_down for m in grp.mods] + [m.lora_up for m in grp.mods]
+    out = _StackedInt8LoRA.apply(x, q, scale, bias, grp, *params)
+    return out.split([m.base.q.shape[0] for m in grp.mods], dim=-1)
 
 
 class DiTBlock(nn.Module):
@@ -93,6 +161,8 @@ class DiTBlock(nn.Module):
         # (each module's base buffers are views of it): one GEMM forward and one dX GEMM backward
         self._stack_bases("qkv", (self.q, self.k, self.v))
         self._stack_bases("ckv", (self.ck, self.cv))
+        # and their LoRA matrices in stacked storage (the modules' Parameters are views of it)
+        self._lora_groups = {"qkv": LoRAGroup((self.q, self.k, self.v)), "ckv": LoRAGroup((self.ck, self.cv))}
 
     def _stack_bases(self, name, mods):
         for part in ("q", "scale", "bias"):
@@ -105,9 +175,10 @@ class DiTBlock(nn.Module):
                 o += n
 
     def _stacked(self, name, x, mods):
-        assert all(m.scale == mods[0].scale for m in mods)
+        grp = self._lora_groups[name]
+        assert all(a is b for a, b in zip(grp.mods, mods))
         return stacked_lora_forward(x, getattr(self, f"{name}_q"), getattr(self, f"{name}_scale"),
-                                    getattr(self, f"{name}_bias"), mods)
+                                    getattr(self, f"{name}_bias"), grp)
 
     def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op, kv=None):
         B, S, _ = xq.shape
