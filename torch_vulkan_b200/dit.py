@@ -222,20 +222,23 @@ class DiTBlock(nn.Module):
 
     def forward(self, x, text, cond):
         kv = self._text_kv_ahead(text)
-        mod = self.ada(F.silu(cond)).unsqueeze(1).chunk(9, dim=-1)
-        sh1, sc1, g1, sh2, sc2, g2, sh3, sc3, g3 = mod
+        ada = self.ada(F.silu(cond))
+        sh1, sc1, g1, sh2, sc2, g2, sh3, sc3, g3 = ada.unsqueeze(1).chunk(9, dim=-1)
+        # one sample: the modulation is the LayerNorm's own affine (one kernel), its three weights 1 + scale
+        # computed by one kernel from the scale chunks (1, 4 and 7 of the nine)
+        ln_w = (1 + ada.view(9, self.h)[1::3]) if x.shape[0] == 1 else None
 
-        def modln(t, sh, sc):
-            if t.shape[0] == 1:  # one sample: the modulation is the LayerNorm's own affine (one kernel)
-                return F.layer_norm(t, (self.h,), weight=(1 + sc).view(self.h), bias=sh.view(self.h), eps=1e-6)
+        def modln(t, sh, sc, i):
+            if ln_w is not None:
+                return F.layer_norm(t, (self.h,), weight=ln_w[i], bias=sh.view(self.h), eps=1e-6)
             return F.layer_norm(t, (self.h,), eps=1e-6) * (1 + sc) + sh
 
         # residual updates x + g * branch as one addcmul kernel
-        h = modln(x, sh1, sc1)
+        h = modln(x, sh1, sc1, 0)
         x = torch.addcmul(x, g1, self._attn(h, h, h, self.q, self.k, self.v, self.o))
-        h = modln(x, sh2, sc2)
+        h = modln(x, sh2, sc2, 1)
         x = torch.addcmul(x, g2, self._attn(h, text, text, self.cq, self.ck, self.cv, self.co, kv=kv))
-        h = modln(x, sh3, sc3)
+        h = modln(x, sh3, sc3, 2)
         # MLP fc2(gelu(fc1(h))) with the GELU (and its backward) in the int8 GEMM epilogues
         mlp = tv.int8_mlp(h, self.fc1.q, self.fc1.scale, self.fc1.bias, self.fc2.q, self.fc2.scale, self.fc2.bias)
         x = torch.addcmul(x, g3, mlp)
