@@ -157,3 +157,46 @@ def test_graphed_step_matches_eager_step():
     lg, pg = run(True)
     assert max(abs(a - b) / abs(a) for a, b in zip(le, lg)) < 1e-3, (le, lg)
     assert rel(pg, pe) < 1e-3
+
+
+def test_stacked_lora_storage_follows_parameter_updates():
+    """The stacked q/k/v and text k/v groups keep their LoRA matrices in stacked storage (each module's
+    Parameter a view of it) and refresh the block-diagonal up-projection every forward: in-place updates of
+    the Parameters (as an optimizer makes them) and fused-AdamW steps reach the next forward of the group,
+    which matches a float64 restatement (dequantised base + x A^T B^T) built from the same Parameters."""
+    from torch_vulkan_b200.dit import DiTStack, LoRATrainer
+
+    def ref_proj(mod, t):
+        t = t.detach().cpu().double()
+        w = oracle.dequant_int8(mod.base.q.cpu(), mod.base.scale.cpu(), torch.bfloat16).double()
+        y = t @ w.t() + mod.base.bias.detach().cpu().double()
+        lo = (t @ mod.lora_down.detach().cpu().double().t()) @ mod.lora_up.detach().cpu().double().t()
+        return y + lo * mod.scale
+
+    def check(b, text, h):
+        for name, inp, mods in (("qkv", h, (b.q, b.k, b.v)), ("ckv", text, (b.ck, b.cv))):
+            outs = b._stacked(name, inp, mods)
+            for o, m in zip(outs, mods):
+                assert rel(o, ref_proj(m, inp)) < 1e-2, name
+        return [o.detach().clone() for o in b._stacked("ckv", text, (b.ck, b.cv))]
+
+    blk, x, text, cond, target = small_block()
+    grp = blk._lora_groups["qkv"]
+    assert blk.k.lora_up.data_ptr() == grp.b[grp.n:].data_ptr() and blk.k.lora_up.is_contiguous()
+    with torch.no_grad():
+        before = check(blk, text, x)
+        for m in (blk.k, blk.cv):
+            m.lora_up.add_(0.2 * torch.randn_like(m.lora_up))
+            m.lora_down.mul_(2.0)
+        after = check(blk, text, x)
+    assert rel(after[1], before[1]) > 1e-2  # the update reached the text-side v projection
+
+    model = DiTStack(blocks=1, seed=3, hidden=256, heads=2, text_dim=128, mlp=512)
+    tr = LoRATrainer(model, lr=1e-2, fused_optimizer=True)
+    with torch.no_grad():
+        start = check(model.blocks[0], text, x)
+    for _ in range(2):
+        tr.step(x, text, cond, target)
+    with torch.no_grad():
+        moved = check(model.blocks[0], text, x)
+    assert rel(moved[0], start[0]) > 1e-4  # the optimizer's updates reached the next forward
