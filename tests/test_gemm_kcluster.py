@@ -1,7 +1,7 @@
 """Split-K GEMMs reduced inside a thread-block cluster (the LoRA projections and weight gradients of the
 DiT block: one of M, N is 16-64, K is long): each CTA of a cluster computes one K slice of a 128x128 tile
 and the cluster sums the fp32 partials through distributed shared memory, with no workspace and no second
-kernel. Checked against float64 in both forms — the cluster reduction (opt-in, B2_GEMM_KCLUSTER=1) and
+kernel. Checked against float64 in both forms — the cluster reduction (the default, B2_GEMM_KCLUSTER=1) and
 the workspace + gemm_splitk_reduce form (=0), each pinned in a child process with the skinny kernel (which
 serves these shapes by default) switched off — over K-major and MN-major operands, ragged M/N, bias with
 alpha/beta, and splits wider than a cluster (which keep the workspace form)."""

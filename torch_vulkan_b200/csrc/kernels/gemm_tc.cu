@@ -1140,17 +1140,18 @@ int kcluster_capacity(int ks) {
   return cap[ks] > 0 ? cap[ks] : 0;
 }
 
-// Split-K reduced inside a cluster (TcParams::kcl), opt-in with B2_GEMM_KCLUSTER=1: GEMMs with few 128x128
-// output tiles and a long K (the LoRA down-projections and weight gradients: N or M = 16-64) whose
+// Split-K reduced inside a cluster (TcParams::kcl; B2_GEMM_KCLUSTER=0 turns it off): GEMMs with few
+// 128x128 output tiles and a long K (the LoRA down-projections and weight gradients: N or M = 16-64) whose
 // splitk_plan split fits a portable cluster (<= 8) take it as clusters of K slices that sum their tile
-// through distributed shared memory, without a workspace or a second kernel. Measured against the default
+// through distributed shared memory, without a workspace or a second kernel. Measured against the
 // workspace + gemm_splitk_reduce form (graphs of back-to-back calls): 1024x2048x48 8.85 -> 7.73 us,
-// 4096x2048x48 10.8 -> 10.2, 4096x8192x16 21.6 -> 20.5, but 6144x1024x48 (MN-major A, 48 clusters of 3)
-// 10.4 -> 10.6 and the DiT configs[4] stack 69.9 -> 71.3 ms, so it is not the default.
+// 4096x2048x48 10.8 -> 10.2, 4096x8192x16 21.6 -> 20.5, 6144x1024x48 (MN-major A, 48 clusters of 3)
+// 10.4 -> 10.6; in the DiT step (graphed, A/B twice each) configs[3] block 0.781 -> 0.776 ms, configs[4]
+// stack 65.37 -> 65.26 ms.
 bool kcluster_plan(const b2_gemm_args* a, const TileChoice& t, int& ks, int& kps) {
   static const bool on = [] {
     const char* e = getenv("B2_GEMM_KCLUSTER");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
   }();
   ks = 1, kps = 0;
   if (!on || a->batch != 1 || t.bn != 128 || t.msub != 1 || a->K <= 0) return false;
