@@ -132,8 +132,8 @@ def test_config4_training_step_runs_and_learns():
     assert all(math.isfinite(v) for v in losses)
     assert losses[-1] < losses[0], losses
     kc = tv.kernel_counts()
-    for op in ("aten::addcmul_", "aten::addcdiv_", "aten::lerp_.Scalar", "b2::int8_linear_dx",
-               "aten::_scaled_dot_product_fused_attention_overrideable_backward"):
+    # the block's attention backward writes into the stacked projection gradients (b2::sdpa_bwd_into)
+    for op in ("aten::addcmul_", "aten::addcdiv_", "aten::lerp_.Scalar", "b2::int8_linear_dx", "b2::sdpa_bwd_into"):
         assert kc.get(op, 0) > 0, (op, kc)
 
 
@@ -200,3 +200,41 @@ def test_stacked_lora_storage_follows_parameter_updates():
     with torch.no_grad():
         moved = check(model.blocks[0], text, x)
     assert rel(moved[0], start[0]) > 1e-4  # the optimizer's updates reached the next forward
+
+
+def test_stacked_attention_gradients_match_split_views():
+    """The DiT block's attention over column blocks of the stacked projection outputs (self-attention: one
+    [B, S, 3 H D] q/k/v tensor; cross-attention: q [B, S, H D] and a stacked [B, Sk, 2 H D] k/v tensor)
+    writes dq, dk, dv straight into blocks of one gradient buffer; output and gradients equal those of
+    F.scaled_dot_product_attention over split views (the same kernels, gradients concatenated by autograd)."""
+    from torch_vulkan_b200.dit import _StackedSDPA
+
+    g = torch.Generator().manual_seed(12)
+    B, S, Sk, H, D = 1, 384, 192, 2, 128
+    hd = H * D
+
+    def heads(t, S_):
+        return t.view(B, S_, H, D).transpose(1, 2)
+
+    # self-attention: q, k, v = blocks 0, 1, 2 of one tensor
+    qkv = torch.randn(B, S, 3 * hd, generator=g).to(torch.bfloat16).cuda().requires_grad_(True)
+    o = _StackedSDPA.apply(qkv, qkv, H, hd, 0, hd, 2 * hd)
+    go = torch.randn(o.shape, generator=g).to(torch.bfloat16).cuda()
+    o.backward(go)
+    ref = qkv.detach().clone().requires_grad_(True)
+    q, k, v = (heads(t, S) for t in ref.split(hd, dim=-1))
+    o_ref = F.scaled_dot_product_attention(q, k, v)
+    o_ref.backward(go)
+    assert rel(o, o_ref) < 1e-3 and rel(qkv.grad, ref.grad) < 1e-3
+
+    # cross-attention: q from its own tensor, k and v from one stacked tensor
+    qt = torch.randn(B, S, hd, generator=g).to(torch.bfloat16).cuda().requires_grad_(True)
+    kv = torch.randn(B, Sk, 2 * hd, generator=g).to(torch.bfloat16).cuda().requires_grad_(True)
+    o = _StackedSDPA.apply(qt, kv, H, hd, 0, 0, hd)
+    go = torch.randn(o.shape, generator=g).to(torch.bfloat16).cuda()
+    o.backward(go)
+    qr, kvr = qt.detach().clone().requires_grad_(True), kv.detach().clone().requires_grad_(True)
+    kr, vr = (heads(t, Sk) for t in kvr.split(hd, dim=-1))
+    o_ref = F.scaled_dot_product_attention(heads(qr, S), kr, vr)
+    o_ref.backward(go)
+    assert rel(o, o_ref) < 1e-3 and rel(qt.grad, qr.grad) < 1e-3 and rel(kv.grad, kvr.grad) < 1e-3

@@ -582,6 +582,48 @@ BwdRet k_sdpa_bwd(const at::Tensor& grad_out, const at::Tensor& query, const at:
   return BwdRet{dq, dk, dv, at::Tensor()};
 }
 
+// The fused attention backward writing dq, dk, dv into caller-provided [B,H,S,D] views (unit stride along
+// D; e.g. column slices of one stacked q/k/v gradient buffer, so the caller needs no concatenation
+// afterwards). Same kernel and arguments as the ATen backward above; scale 0 means 1/sqrt(D).
+void b2_sdpa_bwd_into(const at::Tensor& grad_out, const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+                      const at::Tensor& out, const at::Tensor& lse, double scale, const at::Tensor& dq,
+                      const at::Tensor& dk, const at::Tensor& dv) {
+  const char* name = "b2::sdpa_bwd_into";
+  TORCH_CHECK(attn_supported(query, key, value, std::nullopt, 0.0, false, false),
+              "sdpa_bwd_into: this attention case is not supported by the fused kernel");
+  c10::cuda::CUDAGuard guard(query.device());
+  at::Tensor q = unit_d(query), k = unit_d(key), v = unit_d(value);
+  const int64_t B = q.size(0), H = q.size(1), Sq = q.size(2), Sk = k.size(2), D = q.size(3);
+  for (const at::Tensor* t : {&dq, &dk, &dv}) {
+    TORCH_CHECK(t->dim() == 4 && t->stride(3) == 1 && t->scalar_type() == q.scalar_type() && t->device() == q.device(),
+                "sdpa_bwd_into: gradients must be [B,H,S,D] views with unit stride along D, in q's dtype and device");
+  }
+  TORCH_CHECK(dq.sizes() == q.sizes() && dk.sizes() == k.sizes() && dv.sizes() == value.sizes(),
+              "sdpa_bwd_into: gradient shapes must match q, k, v");
+  at::Tensor dO = unit_d(grad_out.scalar_type() == q.scalar_type() ? grad_out : grad_out.to(q.scalar_type()));
+  at::Tensor o = unit_d(out.scalar_type() == q.scalar_type() ? out : out.to(q.scalar_type()));
+  at::Tensor lse_c = lse.contiguous();
+  at::Tensor delta = at::empty({B, H, Sq}, q.options().dtype(at::kFloat));
+  b2_attn_args a{};
+  a.q = q.data_ptr(), a.k = k.data_ptr(), a.v = v.data_ptr(), a.o = o.data_ptr(), a.lse = lse_c.data_ptr<float>();
+  a.d_o = dO.data_ptr(), a.delta = delta.data_ptr<float>();
+  a.dq = dq.data_ptr(), a.dk = dk.data_ptr(), a.dv = dv.data_ptr();
+  a.B = B, a.H = H, a.Sq = Sq, a.Sk = Sk, a.D = D;
+  fill_strides(a.q_s, q), fill_strides(a.k_s, k), fill_strides(a.v_s, v), fill_strides(a.o_s, o);
+  fill_strides(a.do_s, dO);
+  fill_strides(a.dq_s, dq), fill_strides(a.dk_s, dk), fill_strides(a.dv_s, dv);
+  a.scale = (float)(scale > 0 ? scale : 1.0 / std::sqrt((double)D));
+  a.dtype = dtype_code(q.scalar_type());
+  a.force_simt = (g_force_simt.load() & 2) ? 1 : 0;
+  at::Tensor ws;
+  if (uint64_t wsb = b2_attn_bwd_workspace_bytes(&a)) {
+    ws = at::empty({(int64_t)((wsb + 3) / 4)}, q.options().dtype(at::kFloat));
+    a.workspace = ws.data_ptr();
+  }
+  b2_check(b2_attn_bwd(&a, cur_stream()), name);
+  count(name);
+}
+
 // =============================== int8 ==============================================================
 
 int scale_layout_of(const at::Tensor& q, const at::Tensor& scale) {
@@ -922,6 +964,8 @@ TORCH_LIBRARY(b2, m) {
   m.def("int8_lora_dx(Tensor dy, Tensor q, Tensor scale, Tensor dh, Tensor a) -> Tensor");
   m.def("mse_loss_fwd(Tensor x, Tensor t) -> Tensor");
   m.def("mse_loss_bwd(Tensor grad, Tensor x, Tensor t) -> Tensor");
+  m.def("sdpa_bwd_into(Tensor grad_out, Tensor q, Tensor k, Tensor v, Tensor out, Tensor lse, float scale, "
+        "Tensor(a!) dq, Tensor(b!) dk, Tensor(c!) dv) -> ()");
   m.def("adamw_step_(Tensor(a!)[] params, Tensor[] grads, Tensor(b!)[] exp_avgs, Tensor(c!)[] exp_avg_sqs, float lr, "
         "float beta1, float beta2, float eps, float weight_decay, int step) -> ()");
   m.def("set_enabled(bool on) -> ()", &op_set_enabled);
@@ -942,5 +986,6 @@ TORCH_LIBRARY_IMPL(b2, CUDA, m) {
   m.impl("int8_lora_dx", &b2_int8_lora_dx);
   m.impl("mse_loss_fwd", &b2_mse_loss_fwd_op);
   m.impl("mse_loss_bwd", &b2_mse_loss_bwd_op);
+  m.impl("sdpa_bwd_into", &b2_sdpa_bwd_into);
   m.impl("adamw_step_", &b2_adamw_step_op);
 }

@@ -133,16 +133,52 @@ class _StackedInt8LoRA(torch.autograd.Function):
         return (gx, None, None, None, None, *gdown, *gup)
 
 
-def stacked_lora_forward(x, q, scale, bias, grp: LoRAGroup):
+def stacked_lora_forward(x, q, scale, bias, grp: LoRAGroup, whole=False):
     """LoRAInt8Linear.forward of the modules of a LoRAGroup (they read the same input x), with their frozen
     int8 bases stacked in (q, scale, bias): one down-projection GEMM over the stacked A_i, then one int8
     GEMM whose last reduction block adds the up-projection over the block-diagonal B_i (backward: one dX
     GEMM that also adds dh @ A, and one GEMM each for dh, dA and dB, instead of one of each per module).
-    Returns one [..., out_i] view per module."""
+    Returns one [..., out_i] view per module, or (whole=True) the stacked [..., sum out_i] output."""
     grp.refresh()
     params = [m.lora_down for m in grp.mods] + [m.lora_up for m in grp.mods]
     out = _StackedInt8LoRA.apply(x, q, scale, bias, grp, *params)
+    if whole:
+        return out
     return out.split([m.base.q.shape[0] for m in grp.mods], dim=-1)
+
+
+class _StackedSDPA(torch.autograd.Function):
+    """softmax(q k^T / sqrt(d)) v with q, k, v taken as hd-wide column blocks (at q_off, k_off, v_off) of
+    projection outputs [B, S, *] (the stacked q/k/v output for self-attention; the q output and the stacked
+    k/v output for cross-attention), on the fused attention kernels. The backward writes dq, dk, dv straight
+    into the matching column blocks of one gradient buffer per input (b2::sdpa_bwd_into), so the stacked
+    projections receive their gradient without a concatenation."""
+
+    @staticmethod
+    def _view(t, off, heads, hd):
+        B, S, _ = t.shape
+        return t[..., off:off + hd].view(B, S, heads, hd // heads).transpose(1, 2)
+
+    @staticmethod
+    def forward(ctx, qt, kvt, heads, hd, q_off, k_off, v_off):
+        vw = _StackedSDPA._view
+        q, k, v = vw(qt, q_off, heads, hd), vw(kvt, k_off, heads, hd), vw(kvt, v_off, heads, hd)
+        o, lse = torch.ops.aten._scaled_dot_product_fused_attention_overrideable(q, k, v)[:2]
+        ctx.save_for_backward(qt, kvt, o, lse)
+        ctx.geom, ctx.same = (heads, hd, q_off, k_off, v_off), qt is kvt
+        return o
+
+    @staticmethod
+    def backward(ctx, go):
+        qt, kvt, o, lse = ctx.saved_tensors
+        heads, hd, q_off, k_off, v_off = ctx.geom
+        vw = _StackedSDPA._view
+        gq = torch.empty_like(qt)  # every column block is written: q/k/v (self) or q and k/v (cross)
+        gkv = gq if ctx.same else torch.empty_like(kvt)
+        torch.ops.b2.sdpa_bwd_into(go, vw(qt, q_off, heads, hd), vw(kvt, k_off, heads, hd), vw(kvt, v_off, heads, hd),
+                                   o, lse, 0.0, vw(gq, q_off, heads, hd), vw(gkv, k_off, heads, hd),
+                                   vw(gkv, v_off, heads, hd))
+        return gq, (None if ctx.same else gkv), None, None, None, None, None
 
 
 class DiTBlock(nn.Module):
@@ -174,27 +210,30 @@ class DiTBlock(nn.Module):
                 setattr(m.base, part, full[o:o + n])
                 o += n
 
-    def _stacked(self, name, x, mods):
+    def _stacked(self, name, x, mods, whole=False):
         grp = self._lora_groups[name]
         assert all(a is b for a, b in zip(grp.mods, mods))
         return stacked_lora_forward(x, getattr(self, f"{name}_q"), getattr(self, f"{name}_scale"),
-                                    getattr(self, f"{name}_bias"), grp)
+                                    getattr(self, f"{name}_bias"), grp, whole=whole)
 
     def _attn(self, xq, xkv_k, xkv_v, qp, kp, vp, op, kv=None):
         B, S, _ = xq.shape
         Skv = xkv_k.shape[1]
         # projections that read the same input run as one stacked group (stacked_lora_forward)
-        if kv is not None:  # k, v projected ahead on the side stream
+        hd = self.heads * self.d
+        if kv is not None or (xkv_k is xkv_v and kp is self.ck):  # q, and the stacked text-side k/v output
             q = qp(xq)
-            torch.cuda.current_stream(xq.device).wait_stream(self._side)
-            k, v = kv
-        elif xq is xkv_k and xkv_k is xkv_v and qp is self.q:
-            q, k, v = self._stacked("qkv", xq, (qp, kp, vp))
-        elif xkv_k is xkv_v and kp is self.ck:
-            q = qp(xq)
-            k, v = self._stacked("ckv", xkv_k, (kp, vp))
-        else:
-            q, k, v = qp(xq), kp(xkv_k), vp(xkv_v)
+            if kv is not None:  # projected ahead on the side stream
+                torch.cuda.current_stream(xq.device).wait_stream(self._side)
+            else:
+                kv = self._stacked("ckv", xkv_k, (kp, vp), whole=True)
+            o = _StackedSDPA.apply(q, kv, self.heads, hd, 0, 0, hd)
+            return op(o.transpose(1, 2).reshape(B, S, self.h))
+        if xq is xkv_k and xkv_k is xkv_v and qp is self.q:  # the stacked q/k/v output
+            qkv = self._stacked("qkv", xq, (qp, kp, vp), whole=True)
+            o = _StackedSDPA.apply(qkv, qkv, self.heads, hd, 0, hd, 2 * hd)
+            return op(o.transpose(1, 2).reshape(B, S, self.h))
+        q, k, v = qp(xq), kp(xkv_k), vp(xkv_v)
         q = q.view(B, S, self.heads, self.d).transpose(1, 2)
         k = k.view(B, Skv, self.heads, self.d).transpose(1, 2)
         v = v.view(B, Skv, self.heads, self.d).transpose(1, 2)
@@ -215,9 +254,8 @@ class DiTBlock(nn.Module):
             self._side = torch.cuda.Stream(text.device)
         self._side.wait_stream(main)
         with torch.cuda.stream(self._side):
-            kv = self._stacked("ckv", text, (self.ck, self.cv))
-        for t in kv:  # consumed on the main stream: keep the allocator from reusing them early
-            t.record_stream(main)
+            kv = self._stacked("ckv", text, (self.ck, self.cv), whole=True)
+        kv.record_stream(main)  # consumed on the main stream: keep the allocator from reusing it early
         return kv
 
     def forward(self, x, text, cond):
