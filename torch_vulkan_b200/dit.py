@@ -86,6 +86,12 @@ class LoRAGroup:
             m.lora_down = nn.Parameter(self.a[i * self.r:(i + 1) * self.r])
             m.lora_up = nn.Parameter(self.b[i * self.n:(i + 1) * self.n])
 
+    def diag_blocks(self, full: torch.Tensor) -> torch.Tensor:
+        """[G*N, r] stack of the diagonal [N, r] blocks of a [G*N, G*r] matrix (one strided copy)."""
+        out = torch.empty(self.g * self.n, self.r, dtype=full.dtype, device=full.device)
+        out.view(self.g, self.n, self.r).copy_(full.view(self.g, self.n, self.g, self.r).diagonal(dim1=0, dim2=2).permute(2, 0, 1))
+        return out
+
     def refresh(self):
         """b_bd's diagonal blocks <- B_i * alpha / r (one strided copy; the off-diagonal blocks stay zero)."""
         with torch.no_grad():
@@ -123,9 +129,7 @@ class _StackedInt8LoRA(torch.autograd.Function):
         if ctx.needs_input_grad[0]:  # dy W~ + dh A in one GEMM
             gx = torch.ops.b2.int8_lora_dx(gy2, q, scale, dh, grp.a).view(ctx.x_shape)
         ga = torch.mm(dh.t(), x2)  # [G*r, in]: row block i is module i's lora_down gradient
-        gb_full = torch.mm(gy2.t(), h)  # [G*N, G*r]: only the diagonal blocks are used
-        gb = torch.empty_like(grp.b)
-        gb.view(grp.g, grp.n, grp.r).copy_(gb_full.view(grp.g, grp.n, grp.g, grp.r).diagonal(dim1=0, dim2=2).permute(2, 0, 1))
+        gb = grp.diag_blocks(torch.mm(gy2.t(), h))  # [G*N, G*r] product: only the diagonal blocks are used
         if grp.scale != 1.0:
             gb.mul_(grp.scale)
         gdown = [ga[i * grp.r:(i + 1) * grp.r] for i in range(grp.g)]
